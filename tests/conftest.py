@@ -1,0 +1,36 @@
+"""Shared pytest configuration: the ``gpu`` marker and fixture loading."""
+
+from __future__ import annotations
+
+import glob
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN_DIR = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def golden_names() -> list[str]:
+    return sorted(
+        os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
+    )
+
+
+def load_golden(name: str) -> dict[str, np.ndarray]:
+    with np.load(os.path.join(GOLDEN_DIR, f"{name}.npz")) as data:
+        return {k: data[k] for k in data.files}
+
+
+@pytest.fixture(params=golden_names())
+def golden(request):
+    return request.param, load_golden(request.param)

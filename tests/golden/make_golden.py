@@ -1,0 +1,181 @@
+"""Generate the golden fixtures by running the reference's own sparse-voxel code.
+
+Run from the repository root, with the mlx_diffuser sources available:
+
+    python tests/golden/make_golden.py [--reference /path/to/mlx_diffuser]
+
+MLX cannot be installed here, so the reference files ``src/mlx_diffuser/kernels/sparse.py``
+and ``src/mlx_diffuser/layers/sparse.py`` are executed unmodified on top of the NumPy stand-in
+``oracle/mlx_shim.py``: ``build_neighbor_map``, ``SparseConv3D`` (its pure fallback,
+``use_metal=False``), ``sparse_downsample`` and ``sparse_upsample``. Their outputs are written
+to ``tests/golden/*.npz``. The fixtures travel with the repository; the reference does not.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import os
+import sys
+import types
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from mlx_diffuser_b200 import scenes  # noqa: E402
+from oracle import mlx_shim  # noqa: E402
+
+
+def load_reference(reference_root: str):
+    """Import the reference's two hot-path modules under the shim; returns (kernels, layers)."""
+
+    mlx_shim.install()
+    src = os.path.join(reference_root, "src", "mlx_diffuser")
+    for name, path in (
+        ("mlx_diffuser", src),
+        ("mlx_diffuser.kernels", os.path.join(src, "kernels")),
+        ("mlx_diffuser.layers", os.path.join(src, "layers")),
+    ):
+        pkg = types.ModuleType(name)
+        pkg.__path__ = [path]
+        sys.modules[name] = pkg
+
+    def load(name: str, path: str):
+        spec = importlib.util.spec_from_file_location(name, path)
+        module = importlib.util.module_from_spec(spec)
+        sys.modules[name] = module
+        spec.loader.exec_module(module)
+        return module
+
+    kernels_sparse = load("mlx_diffuser.kernels.sparse", os.path.join(src, "kernels", "sparse.py"))
+    sys.modules["mlx_diffuser.kernels"].sparse_conv3d = kernels_sparse.sparse_conv3d
+    layers_sparse = load("mlx_diffuser.layers.sparse", os.path.join(src, "layers", "sparse.py"))
+    return kernels_sparse, layers_sparse
+
+
+def run_case(ref, coords, features, weight, bias, *, kernel_size=3, dilation=1, factors=(2,),
+             spatial_shape=None, extra_maps=()):
+    """Run the reference path on one input and collect every output as numpy arrays."""
+
+    _, L = ref
+    mx = sys.modules["mlx.core"]
+    out: dict[str, np.ndarray] = {
+        "coords": coords.astype(np.int32),
+        "features": features.astype(np.float32),
+        "weight": weight.astype(np.float32),
+        "bias": bias.astype(np.float32),
+        "kernel_size": np.int32(kernel_size),
+        "dilation": np.int32(dilation),
+    }
+    tensor = L.SparseTensor(mx.array(features), mx.array(coords), spatial_shape=spatial_shape)
+    out["batch_size"] = np.int32(tensor.batch_size)
+    out["spatial_shape"] = np.asarray(tensor.spatial_shape, np.int32)
+    out["nbr"] = np.asarray(L.build_neighbor_map(tensor.coords, kernel_size, dilation), np.int32)
+    for i, (ks, dl) in enumerate(extra_maps):
+        out[f"nbr_extra{i}"] = np.asarray(L.build_neighbor_map(tensor.coords, ks, dl), np.int32)
+        out[f"nbr_extra{i}_kernel"] = np.asarray(ks if not isinstance(ks, int) else (ks,) * 3)
+        out[f"nbr_extra{i}_dilation"] = np.asarray(dl if not isinstance(dl, int) else (dl,) * 3)
+    conv = L.SparseConv3D(weight.shape[-1], weight.shape[0], kernel_size, dilation=dilation,
+                          use_metal=False)
+    conv.conv.weight = mx.array(weight)
+    conv.conv.bias = mx.array(bias)
+    out["conv_out"] = np.asarray(conv(tensor).features, np.float32)
+    for f in factors:
+        down = L.sparse_downsample(tensor, f)
+        up = L.sparse_upsample(down, f)
+        out[f"down{f}_coords"] = np.asarray(down.coords, np.int32)
+        out[f"down{f}_inverse"] = np.asarray(
+            down.cache[f"upsample_{f}_{down.scale}"][1], np.int32
+        ).reshape(-1)
+        out[f"down{f}_features"] = np.asarray(down.features, np.float32)
+        out[f"down{f}_spatial_shape"] = np.asarray(down.spatial_shape, np.int32)
+        out[f"down{f}_scale"] = np.asarray(down.scale, np.int32)
+        out[f"up{f}_features"] = np.asarray(up.features, np.float32)
+    return out
+
+
+def cases(ref):
+    rng = np.random.default_rng(1234)
+    yield "ref_test_four_points", run_case(
+        ref,
+        np.array([[0, 0, 0, 0], [0, 0, 0, 1], [0, 0, 1, 0], [0, 1, 0, 0]], np.int32),
+        np.arange(12, dtype=np.float32).reshape(4, 3),
+        rng.uniform(-0.3, 0.3, (2, 3, 3, 3, 3)).astype(np.float32),
+        np.array([0.5, -0.25], np.float32),
+    )
+    block = np.array([[0, z, y, x] for z in range(2) for y in range(2) for x in range(2)], np.int32)
+    yield "ref_test_block2", run_case(
+        ref,
+        block,
+        np.arange(16, dtype=np.float32).reshape(8, 2),
+        rng.uniform(-0.3, 0.3, (2, 3, 3, 3, 2)).astype(np.float32),
+        np.zeros(2, np.float32),
+        spatial_shape=(2, 2, 2),
+    )
+    # duplicates, negative coordinates, three batch elements, odd factors
+    c = rng.integers(-6, 6, size=(400, 4)).astype(np.int32)
+    c[:, 0] = rng.integers(0, 3, size=400)
+    c = np.concatenate([c, c[rng.integers(0, 400, 40)]], axis=0)  # 40 duplicate rows
+    yield "duplicates_negative", run_case(
+        ref,
+        c,
+        rng.standard_normal((len(c), 5)).astype(np.float32),
+        rng.standard_normal((7, 3, 3, 3, 5)).astype(np.float32) * 0.1,
+        rng.standard_normal(7).astype(np.float32),
+        factors=(2, 3),
+        extra_maps=(((3, 1, 5), (2, 1, 1)), (1, 1), (5, 2)),
+    )
+    s = scenes.shell(16, 5.5, 2.0, 1.0, seed=7)
+    s = scenes.batched([s, scenes.shell(16, 6.0, 2.0, 1.0, seed=8)])
+    yield "shell16_pair", run_case(
+        ref,
+        s,
+        scenes.normal_features(len(s), 16, seed=11),
+        scenes.conv_weight(24, 16, 3, seed=12),
+        rng.standard_normal(24).astype(np.float32) * 0.1,
+    )
+    s = scenes.shell(20, 7.0, 2.5, 1.0, seed=21)
+    yield "shell20_kernel5", run_case(
+        ref,
+        s,
+        scenes.normal_features(len(s), 8, seed=22),
+        scenes.conv_weight(8, 8, 5, seed=23),
+        np.zeros(8, np.float32),
+        kernel_size=5,
+        dilation=1,
+    )
+    s = scenes.shell(24, 8.0, 2.5, 1.0, seed=31)
+    yield "shell24_dilation2", run_case(
+        ref,
+        s,
+        scenes.normal_features(len(s), 64, seed=32),
+        scenes.conv_weight(64, 64, 3, seed=33),
+        rng.standard_normal(64).astype(np.float32) * 0.1,
+        dilation=2,
+    )
+    s = scenes.shell32(seed=41)
+    yield "shell32_c64", run_case(
+        ref,
+        s,
+        scenes.normal_features(len(s), 64, seed=42),
+        scenes.conv_weight(64, 64, 3, seed=43),
+        np.zeros(64, np.float32),
+    )
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", default=os.environ.get("MLX_DIFFUSER_REF", "/root/reference"))
+    args = parser.parse_args()
+    ref = load_reference(args.reference)
+    for name, data in cases(ref):
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **data)
+        print(f"{name}: N={len(data['coords'])} -> {os.path.relpath(path, ROOT)}")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,104 @@
+"""Pin the CPU oracle against fixtures produced by the reference's own sparse-voxel code.
+
+The fixtures under ``tests/golden`` were made by ``tests/golden/make_golden.py``, which runs
+mlx_diffuser's ``layers/sparse.py`` and ``kernels/sparse.py`` unmodified (fallback conv path).
+Integer outputs must match bit-exactly; float32 features to float32 summation-order noise.
+"""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import sparse_oracle as O
+from tests.conftest import load_golden
+
+
+def _maps(g):
+    yield int(g["kernel_size"]), int(g["dilation"]), g["nbr"]
+    i = 0
+    while f"nbr_extra{i}" in g:
+        yield tuple(g[f"nbr_extra{i}_kernel"]), tuple(g[f"nbr_extra{i}_dilation"]), g[f"nbr_extra{i}"]
+        i += 1
+
+
+def test_kernel_map_bit_exact(golden):
+    _, g = golden
+    for ks, dl, want in _maps(g):
+        ks = ks if isinstance(ks, int) else tuple(int(v) for v in ks)
+        dl = dl if isinstance(dl, int) else tuple(int(v) for v in dl)
+        assert np.array_equal(O.build_neighbor_map(g["coords"], ks, dl), want)
+        if len(g["coords"]) <= 2500:
+            assert np.array_equal(O.build_neighbor_map_dict(g["coords"], ks, dl), want)
+
+
+def test_conv_matches_reference_fallback(golden):
+    _, g = golden
+    w = O.spconv_weight_to_kio(g["weight"])
+    got = O.sparse_conv3d(g["features"], g["nbr"], w, g["bias"])
+    np.testing.assert_allclose(got, g["conv_out"], rtol=1e-5, atol=1e-5)
+
+
+def test_downsample_upsample_bit_exact(golden):
+    _, g = golden
+    factors = sorted(int(k[4:-7]) for k in g if k.startswith("down") and k.endswith("_coords"))
+    assert factors
+    for f in factors:
+        coords, inverse = O.downsample_coords(g["coords"], f)
+        assert np.array_equal(coords, g[f"down{f}_coords"])
+        assert np.array_equal(inverse, g[f"down{f}_inverse"])
+        pooled = O.downsample_features(g["features"], inverse, len(coords))
+        # np.add.at sums in row order, exactly like the reference's scatter-add
+        assert np.array_equal(pooled, g[f"down{f}_features"])
+        assert np.array_equal(O.upsample_features(pooled, inverse), g[f"up{f}_features"])
+        shape = O.downsample_spatial_shape(tuple(g["spatial_shape"]), f)
+        assert shape == tuple(g[f"down{f}_spatial_shape"])
+
+
+def test_reference_block_pool_divides_by_count_plus_one():
+    """``tests/test_trellis.py:147-161`` of the reference: a 2^3 block pools to sum / 9."""
+
+    g = load_golden("ref_test_block2")
+    assert g["down2_coords"].shape == (1, 4)
+    np.testing.assert_allclose(g["up2_features"], np.broadcast_to(g["features"].sum(0) / 9, (8, 2)))
+
+
+def test_offsets_order_matches_reference():
+    offs = O.kernel_offsets(3)
+    assert len(offs) == 27 and offs[0] == (-1, -1, -1) and offs[13] == (0, 0, 0)
+    assert offs[1] == (-1, -1, 0) and offs[9] == (0, -1, -1)
+    with pytest.raises(ValueError):
+        O.kernel_offsets(4)
+
+
+REF = os.environ.get("MLX_DIFFUSER_REF", "/root/reference")
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "src", "mlx_diffuser")),
+                    reason="reference sources not present")
+def test_oracle_against_live_reference_random_cases():
+    """Where the reference sources exist, run them under the NumPy shim on fresh random
+    inputs (duplicates, negatives, several batches) and compare with the oracle."""
+
+    from tests.golden.make_golden import load_reference, run_case
+
+    ref = load_reference(REF)
+    rng = np.random.default_rng(99)
+    for _ in range(3):
+        n = int(rng.integers(1, 300))
+        c = rng.integers(-4, 5, size=(n, 4)).astype(np.int32)
+        c[:, 0] = rng.integers(0, 3, size=n)
+        feats = rng.standard_normal((n, 3)).astype(np.float32)
+        w = rng.standard_normal((2, 3, 3, 3, 3)).astype(np.float32)
+        b = rng.standard_normal(2).astype(np.float32)
+        g = run_case(ref, c, feats, w, b, factors=(2, 4))
+        assert np.array_equal(O.build_neighbor_map(c, 3), g["nbr"])
+        np.testing.assert_allclose(
+            O.sparse_conv3d(feats, g["nbr"], O.spconv_weight_to_kio(w), b), g["conv_out"],
+            rtol=1e-5, atol=1e-5)
+        for f in (2, 4):
+            coords, inverse = O.downsample_coords(c, f)
+            assert np.array_equal(coords, g[f"down{f}_coords"])
+            assert np.array_equal(inverse, g[f"down{f}_inverse"])
