@@ -1,0 +1,150 @@
+/*
+ * sparsevox -- C ABI of the B200 (sm_100a) sparse-voxel library that replaces
+ * mlx_diffuser's TRELLIS sparse-voxel hot path.
+ *
+ * Every entry point takes plain device pointers and sizes, never a framework type, and
+ * enqueues its work on the given CUDA stream (`sv_stream_t` is a `cudaStream_t`). Outputs
+ * and scratch ("workspace") are allocated by the caller; the library allocates nothing.
+ * Functions return an `sv_status`; on failure `sv_last_error()` (thread-local) describes it.
+ * Kernels that can detect a data error at run time (hash table full, neighbour index out of
+ * range, a bounded wait that expired) OR a bit into the optional device word `status`.
+ *
+ * Reference interfaces replaced (paths relative to the mlx_diffuser project root):
+ *   src/mlx_diffuser/layers/sparse.py:146-175   build_neighbor_map
+ *   src/mlx_diffuser/layers/sparse.py:217-235   SparseConv3D.__call__
+ *   src/mlx_diffuser/kernels/sparse.py:58-105   sparse_conv3d (+ the Metal kernel :9-36)
+ *   src/mlx_diffuser/layers/sparse.py:245-284   sparse_downsample
+ *   src/mlx_diffuser/layers/sparse.py:287-295   sparse_upsample
+ */
+#ifndef SPARSEVOX_H_
+#define SPARSEVOX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SV_API __attribute__((visibility("default")))
+#else
+#define SV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* sv_stream_t; /* cudaStream_t */
+
+typedef enum sv_status {
+  SV_OK = 0,
+  SV_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad enum value */
+  SV_ERR_BAD_SHAPE = 2,        /* shape contract violated (the reference raises ValueError) */
+  SV_ERR_BAD_DTYPE = 3,
+  SV_ERR_TABLE_FULL = 4,       /* coordinate hash table too small for the input */
+  SV_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed */
+  SV_ERR_UNSUPPORTED = 6,      /* valid input outside what this build implements */
+  SV_ERR_WORKSPACE = 7         /* workspace pointer null or smaller than required */
+} sv_status;
+
+typedef enum sv_dtype { SV_FLOAT32 = 0, SV_FLOAT16 = 1, SV_BFLOAT16 = 2 } sv_dtype;
+
+/* Weight layouts accepted by the convolution.
+ *  SV_WEIGHT_KIO: (K, Cin, Cout), the view `sparse_conv3d` receives
+ *                 (src/mlx_diffuser/kernels/sparse.py:72).
+ *  SV_WEIGHT_OKI: (Cout, kD, kH, kW, Cin), spconv's checkpoint layout held by
+ *                 `_SparseConv3DCore.weight` (src/mlx_diffuser/layers/sparse.py:178-193). */
+typedef enum sv_weight_layout { SV_WEIGHT_KIO = 0, SV_WEIGHT_OKI = 1 } sv_weight_layout;
+
+/* Convolution algorithm. AUTO picks the tcgen05 tensor-core kernel when the shape allows it
+ * (fp16/bf16, Cin % 64 == 0, Cout % 32 == 0, K <= 27, 16-byte aligned pointers) and the
+ * CUDA-core kernel otherwise. */
+typedef enum sv_conv_algo { SV_CONV_AUTO = 0, SV_CONV_SIMT = 1, SV_CONV_TCGEN05 = 2 } sv_conv_algo;
+
+/* Bits a kernel ORs into the optional device status word. */
+#define SV_DEVICE_TABLE_FULL 0x1    /* an insert gave up after probing every slot */
+#define SV_DEVICE_BAD_INDEX 0x2     /* a neighbour / row index out of range, treated as empty */
+#define SV_DEVICE_WAIT_TIMEOUT 0x4  /* a bounded in-kernel wait expired; output invalid */
+
+SV_API const char* sv_last_error(void);
+SV_API int sv_abi_version(void);
+
+/* ---- kernel map (build_neighbor_map, src/mlx_diffuser/layers/sparse.py:146-175) -------- */
+
+/* Slots of the open-addressing coordinate table used for n rows (a power of two >= 2n). */
+SV_API int64_t sv_kmap_table_slots(int64_t n);
+/* Workspace bytes for sv_kmap_build with `table_slots` slots (4 bytes per slot). */
+SV_API size_t sv_kmap_workspace_bytes(int64_t table_slots);
+
+/* nbr[p, k] = the row of (b, c1+d1, c2+d2, c3+d3), or -1, for the offsets (d1, d2, d3) of a
+ * kernel (kernel[0..2] odd) and dilation in the reference's order: offset index
+ * k = (a*kernel[1] + b)*kernel[2] + c with d = ((a - kernel[0]/2)*dilation[0], ...), added to
+ * coords columns 1, 2, 3. Duplicate coordinate rows resolve to the largest row index.
+ * coords: [n, 4] int32 (batch, c1, c2, c3), 16-byte aligned; nbr: [n, kernel volume] int32.
+ * The hash table lives in `workspace` (sv_kmap_workspace_bytes(table_slots) bytes). A table
+ * with fewer slots than distinct rows is detected on the device: SV_DEVICE_TABLE_FULL is ORed
+ * into `status` (the return value only reports what the host can see). */
+SV_API int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                         const int32_t dilation[3], int32_t* nbr, int64_t table_slots,
+                         void* workspace, size_t workspace_bytes, int32_t* status,
+                         sv_stream_t stream);
+
+/* Row schedule for the tensor-core convolution: a permutation of 0..n-1 that groups rows with
+ * equal neighbour-validity masks (stable, so rows with one mask keep their spatial order).
+ * Needs kvol <= 32. Workspace: sv_conv_plan_workspace_bytes(n). */
+SV_API size_t sv_conv_plan_workspace_bytes(int64_t n);
+SV_API int sv_conv_plan(const int32_t* nbr, int64_t n, int kvol, int32_t* row_order,
+                        void* workspace, size_t workspace_bytes, sv_stream_t stream);
+
+/* ---- convolution (sparse_conv3d / SparseConv3D.__call__) ------------------------------ */
+
+/* out[p, o] = bias[o] + sum_k sum_i features[nbr[p,k], i] * W[k, i, o] over nbr[p,k] >= 0,
+ * accumulated in fp32 and rounded once to `dtype` (the Metal kernel's semantics,
+ * src/mlx_diffuser/kernels/sparse.py:14-34). features [n, cin], weight in `layout`, bias
+ * [cout] (nullable = zero), out [n, cout]; all of `dtype`. row_order (nullable) is a
+ * permutation from sv_conv_plan that only changes the schedule, never the result.
+ * A KIO weight on the tensor-core path is repacked into `workspace`
+ * (sv_conv3d_workspace_bytes bytes); otherwise workspace may be null. */
+SV_API size_t sv_conv3d_workspace_bytes(int64_t n, int cin, int cout, int kvol, int dtype,
+                                        int layout, int algo);
+SV_API int sv_conv3d_forward(const void* features, int64_t n, int cin, const int32_t* nbr,
+                             int kvol, const int32_t* row_order, const void* weight, int layout,
+                             const void* bias, int cout, int dtype, void* out, int algo,
+                             void* workspace, size_t workspace_bytes, int32_t* status,
+                             sv_stream_t stream);
+
+/* Repack a (K, Cin, Cout) weight into spconv's (Cout, K, Cin) layout. */
+SV_API int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int cout, int dtype,
+                                void* w_oki, sv_stream_t stream);
+
+/* ---- pooling (sparse_downsample / sparse_upsample) ------------------------------------- */
+
+/* Workspace bytes for sv_downsample_coords on n rows. */
+SV_API size_t sv_downsample_workspace_bytes(int64_t n);
+
+/* new coords = unique rows of (b, c1 // f, c2 // f, c3 // f) (floor division) in
+ * lexicographic signed order, as np.unique(axis=0) returns them
+ * (src/mlx_diffuser/layers/sparse.py:250-253); inverse[i] = coarse row of fine row i.
+ * Also emits the fine rows grouped by coarse row (sorted_rows [n], stable) and the group
+ * boundaries seg_offsets [m + 1], which sv_downsample_features consumes.
+ * out_coords must hold n rows. The coarse count m is written to *out_m (host memory); this
+ * call synchronises `stream`. */
+SV_API int sv_downsample_coords(const int32_t* coords, int64_t n, int factor,
+                                int32_t* out_coords, int32_t* inverse, int32_t* sorted_rows,
+                                int32_t* seg_offsets, int64_t* out_m, void* workspace,
+                                size_t workspace_bytes, sv_stream_t stream);
+
+/* out[j] = (sum of features over the fine rows of coarse row j) / (count_j + 1)
+ * (src/mlx_diffuser/layers/sparse.py:254-266); fp32 sums in fine-row order. */
+SV_API int sv_downsample_features(const void* features, int64_t n, int channels, int dtype,
+                                  const int32_t* sorted_rows, const int32_t* seg_offsets,
+                                  int64_t m, void* out, sv_stream_t stream);
+
+/* out[i] = coarse[inverse[i]] (src/mlx_diffuser/layers/sparse.py:295). */
+SV_API int sv_upsample_features(const void* coarse, int64_t m, int channels, int dtype,
+                                const int32_t* inverse, int64_t n, void* out, int32_t* status,
+                                sv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSEVOX_H_ */

@@ -1,0 +1,126 @@
+// C-ABI entry points for the convolution, weight repacking and error reporting.
+#include <string>
+
+#include "conv.h"
+
+namespace sv {
+
+namespace {
+thread_local std::string g_last_error;
+
+// Tiled transpose of a rows x cols matrix (element type E): the (K*Cin) x Cout weight view
+// becomes Cout x (K*Cin), i.e. (K, Cin, Cout) -> (Cout, K, Cin).
+template <typename E>
+__global__ void transpose_kernel(const E* __restrict__ in, int64_t rows, int64_t cols,
+                                 E* __restrict__ out) {
+  __shared__ E tile[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = in[r * cols + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) out[c * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+int transpose(const void* in, int64_t rows, int64_t cols, int esize, void* out, cudaStream_t s) {
+  if (rows == 0 || cols == 0) return SV_OK;
+  const dim3 block(32, 8), grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32));
+  if ((rows + 31) / 32 > 65535) SV_FAIL(SV_ERR_UNSUPPORTED, "weight too large to repack");
+  if (esize == 4)
+    transpose_kernel<uint32_t><<<grid, block, 0, s>>>(static_cast<const uint32_t*>(in), rows,
+                                                       cols, static_cast<uint32_t*>(out));
+  else
+    transpose_kernel<uint16_t><<<grid, block, 0, s>>>(static_cast<const uint16_t*>(in), rows,
+                                                       cols, static_cast<uint16_t*>(out));
+  SV_LAUNCH_CHECK();
+  return SV_OK;
+}
+
+bool valid_dtype(int d) { return d == SV_FLOAT32 || d == SV_FLOAT16 || d == SV_BFLOAT16; }
+
+// Would the AUTO/TCGEN05 choice take the tensor-core kernel for this shape (after a repack)?
+bool tc_path(const ConvArgs& a, int algo) {
+  if (algo == SV_CONV_SIMT) return false;
+  ConvArgs b = a;
+  b.layout = SV_WEIGHT_OKI;  // a KIO weight is repacked into an aligned workspace
+  if (a.layout == SV_WEIGHT_KIO) b.weight = reinterpret_cast<const void*>(uintptr_t(256));
+  return conv_tc_supported(b);
+}
+
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+}  // namespace sv
+
+using namespace sv;
+
+extern "C" const char* sv_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int sv_abi_version(void) { return 1; }
+
+extern "C" size_t sv_conv3d_workspace_bytes(int64_t n, int cin, int cout, int kvol, int dtype,
+                                            int layout, int algo) {
+  if (layout != SV_WEIGHT_KIO || !valid_dtype(dtype)) return 0;
+  ConvArgs a{};
+  a.n = n;
+  a.cin = cin;
+  a.cout = cout;
+  a.kvol = kvol;
+  a.dtype = dtype;
+  a.layout = layout;
+  a.features = a.out = reinterpret_cast<void*>(uintptr_t(256));
+  if (!tc_path(a, algo)) return 0;
+  return align_up((size_t)kvol * cin * cout * dtype_size(dtype), 256);
+}
+
+extern "C" int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int cout, int dtype,
+                                    void* w_oki, sv_stream_t stream) {
+  if (!valid_dtype(dtype)) SV_FAIL(SV_ERR_BAD_DTYPE, "sv_weight_kio_to_oki: unknown dtype");
+  if (kvol < 0 || cin < 0 || cout < 0) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "negative size");
+  if ((int64_t)kvol * cin * cout == 0) return SV_OK;
+  if (!w_kio || !w_oki) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_weight_kio_to_oki: null pointer");
+  return transpose(w_kio, (int64_t)kvol * cin, cout, dtype_size(dtype), w_oki, to_stream(stream));
+}
+
+extern "C" int sv_conv3d_forward(const void* features, int64_t n, int cin, const int32_t* nbr,
+                                 int kvol, const int32_t* row_order, const void* weight,
+                                 int layout, const void* bias, int cout, int dtype, void* out,
+                                 int algo, void* workspace, size_t workspace_bytes,
+                                 int32_t* status, sv_stream_t stream) {
+  if (n < 0 || cin < 0 || cout < 0 || kvol < 1)
+    SV_FAIL(SV_ERR_BAD_SHAPE, "sv_conv3d_forward: negative size or empty kernel");
+  if (!valid_dtype(dtype)) SV_FAIL(SV_ERR_BAD_DTYPE, "sv_conv3d_forward: unknown dtype");
+  if (layout != SV_WEIGHT_KIO && layout != SV_WEIGHT_OKI)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward: unknown weight layout");
+  if (algo != SV_CONV_AUTO && algo != SV_CONV_SIMT && algo != SV_CONV_TCGEN05)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward: unknown algorithm");
+  if (n == 0 || cout == 0) return SV_OK;
+  if (!features || !nbr || !out || (!weight && cin > 0))
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward: null pointer");
+  cudaStream_t s = to_stream(stream);
+  ConvArgs a{features, n, cin, nbr, kvol, row_order, weight, layout, bias, cout, dtype, out,
+             status};
+  const bool use_tc = tc_path(a, algo) && aligned16(weight);
+  if (algo == SV_CONV_TCGEN05 && !use_tc)
+    SV_FAIL(SV_ERR_UNSUPPORTED,
+            "tcgen05 convolution needs fp16/bf16, Cin % 64 == 0, Cout % 32 == 0, kernel volume "
+            "<= 27 and 16-byte aligned features/weight/out");
+  if (!use_tc) return conv_simt_launch(a, s);
+  if (layout == SV_WEIGHT_KIO) {
+    const size_t need = (size_t)kvol * cin * cout * dtype_size(dtype);
+    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+      SV_FAIL(SV_ERR_WORKSPACE,
+              "sv_conv3d_forward: a (K, Cin, Cout) weight on the tcgen05 path needs "
+              "sv_conv3d_workspace_bytes() of workspace");
+    int rc = transpose(weight, (int64_t)kvol * cin, cout, dtype_size(dtype), workspace, s);
+    if (rc != SV_OK) return rc;
+    a.weight = workspace;
+    a.layout = SV_WEIGHT_OKI;
+  }
+  return conv_tc_launch(a, s);
+}

@@ -1,0 +1,156 @@
+// Output-stationary sparse convolution on the CUDA cores (fp32 FFMA).
+//
+// Computes the Metal kernel's result (src/mlx_diffuser/kernels/sparse.py:14-34): for every
+// output row, bias plus the sum over kernel offsets with a valid neighbour of the neighbour's
+// feature row times W[k], accumulated in fp32 and rounded once. It serves fp32 features and
+// the shapes the tcgen05 kernel does not take (Cin not a multiple of 64, Cout not a multiple
+// of 32, kernel volume above 27).
+//
+// A CTA owns a 64-row x 64-column output tile. For each offset it stages the 64 gathered
+// neighbour indices; offsets with no valid neighbour in the tile are skipped as a whole. The
+// K loop stages a gathered 64x16 slab of features and a 16x64 slab of W[k] in shared memory;
+// each thread accumulates a 4x4 block.
+#include "conv.h"
+
+namespace sv {
+namespace {
+
+constexpr int SBM = 64, SBN = 64, SBK = 16;
+
+template <typename T, int LAYOUT>
+__global__ void __launch_bounds__(256) conv_simt_kernel(
+    const T* __restrict__ feat, int64_t n, int cin, const int32_t* __restrict__ nbr, int kvol,
+    const int32_t* __restrict__ row_order, const T* __restrict__ w, const T* __restrict__ bias,
+    int cout, T* __restrict__ out, int32_t* status) {
+  __shared__ __align__(16) float As[SBK][SBM];
+  __shared__ __align__(16) float Bs[SBK][SBN];
+  __shared__ int32_t s_src[SBM];
+  __shared__ int32_t s_orow[SBM];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t row0 = (int64_t)blockIdx.x * SBM;
+  const int col0 = blockIdx.y * SBN;
+  if (tid < SBM) {
+    const int64_t g = row0 + tid;
+    int32_t o = -1;
+    if (g < n) {
+      o = row_order ? __ldg(&row_order[g]) : (int32_t)g;
+      if (o < 0 || o >= n) {
+        report(status, SV_DEVICE_BAD_INDEX);
+        o = -1;
+      }
+    }
+    s_orow[tid] = o;
+  }
+  __syncthreads();
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+  for (int k = 0; k < kvol; ++k) {
+    int valid = 0;
+    if (tid < SBM) {
+      const int32_t o = s_orow[tid];
+      int32_t src = o >= 0 ? __ldg(&nbr[(int64_t)o * kvol + k]) : -1;
+      if (src >= n) {
+        report(status, SV_DEVICE_BAD_INDEX);
+        src = -1;
+      }
+      s_src[tid] = src;
+      valid = src >= 0;
+    }
+    if (!__syncthreads_or(valid)) continue;
+    for (int c0 = 0; c0 < cin; c0 += SBK) {
+#pragma unroll
+      for (int i = 0; i < (SBM * SBK) / 256; ++i) {
+        const int e = tid + i * 256;
+        const int r = e / SBK, kk = e % SBK;
+        const int32_t src = s_src[r];
+        const int ci = c0 + kk;
+        As[kk][r] = (src >= 0 && ci < cin) ? to_f32(feat[(int64_t)src * cin + ci]) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < (SBK * SBN) / 256; ++i) {
+        const int e = tid + i * 256;
+        int kk, j;
+        if (LAYOUT == SV_WEIGHT_KIO) {
+          kk = e / SBN;
+          j = e % SBN;
+        } else {
+          kk = e % SBK;
+          j = e / SBK;
+        }
+        const int ci = c0 + kk, co = col0 + j;
+        float v = 0.f;
+        if (ci < cin && co < cout) {
+          v = LAYOUT == SV_WEIGHT_KIO ? to_f32(w[((int64_t)k * cin + ci) * cout + co])
+                                      : to_f32(w[((int64_t)co * kvol + k) * cin + ci]);
+        }
+        Bs[kk][j] = v;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < SBK; ++kk) {
+        const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+        const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+        const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      }
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int32_t o = s_orow[ty * 4 + i];
+    if (o < 0) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int co = col0 + tx * 4 + j;
+      if (co < cout) {
+        const float b = bias ? to_f32(bias[co]) : 0.f;
+        out[(int64_t)o * cout + co] = from_f32<T>(acc[i][j] + b);
+      }
+    }
+  }
+}
+
+template <typename T>
+int launch_typed(const ConvArgs& a, cudaStream_t s) {
+  const dim3 grid((unsigned)((a.n + SBM - 1) / SBM), (unsigned)((a.cout + SBN - 1) / SBN));
+  const T* f = static_cast<const T*>(a.features);
+  const T* w = static_cast<const T*>(a.weight);
+  const T* b = static_cast<const T*>(a.bias);
+  T* o = static_cast<T*>(a.out);
+  if (a.layout == SV_WEIGHT_KIO)
+    conv_simt_kernel<T, SV_WEIGHT_KIO><<<grid, 256, 0, s>>>(f, a.n, a.cin, a.nbr, a.kvol,
+                                                            a.row_order, w, b, a.cout, o,
+                                                            a.status);
+  else
+    conv_simt_kernel<T, SV_WEIGHT_OKI><<<grid, 256, 0, s>>>(f, a.n, a.cin, a.nbr, a.kvol,
+                                                            a.row_order, w, b, a.cout, o,
+                                                            a.status);
+  SV_LAUNCH_CHECK();
+  return SV_OK;
+}
+
+}  // namespace
+
+int conv_simt_launch(const ConvArgs& a, cudaStream_t s) {
+  if (a.n == 0 || a.cout == 0) return SV_OK;
+  if ((a.n + SBM - 1) / SBM > INT32_MAX || (a.cout + SBN - 1) / SBN > 65535)
+    SV_FAIL(SV_ERR_UNSUPPORTED, "conv: problem too large for the grid");
+  switch (a.dtype) {
+    case SV_FLOAT32: return launch_typed<float>(a, s);
+    case SV_FLOAT16: return launch_typed<__half>(a, s);
+    case SV_BFLOAT16: return launch_typed<__nv_bfloat16>(a, s);
+  }
+  SV_FAIL(SV_ERR_BAD_DTYPE, "conv: unknown dtype");
+}
+
+}  // namespace sv

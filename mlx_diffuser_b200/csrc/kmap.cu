@@ -1,0 +1,193 @@
+// Kernel-map construction: coordinate hash table, K-offset neighbour probe, and the
+// mask-grouped row schedule for the tensor-core convolution.
+//
+// Restates build_neighbor_map (src/mlx_diffuser/layers/sparse.py:146-175) on the GPU:
+//  * the reference's dict keyed by the 4-tuple (b, c1, c2, c3) becomes an open-addressing
+//    table whose slots hold only a row index (4 bytes); a slot's key is the coordinate row it
+//    points at, so keys are exact for every int32 value (no packing, no range limit);
+//  * "a later duplicate overwrites an earlier one" (the dict comprehension, :159) becomes
+//    atomicMax on the slot: the largest row index among equal rows wins;
+//  * offsets are enumerated in the reference's order (:160-169); a neighbour coordinate that
+//    leaves the int32 range simply misses, as a Python dict lookup of that tuple would.
+#include <cub/device/device_radix_sort.cuh>
+
+#include "common.cuh"
+
+namespace sv {
+namespace {
+
+__device__ __forceinline__ uint32_t hash_coord(int b, int x, int y, int z) {
+  uint64_t h = (uint64_t)(uint32_t)b * 0x9E3779B97F4A7C15ull;
+  h += (uint64_t)(uint32_t)x * 0xC2B2AE3D27D4EB4Full;
+  h += (uint64_t)(uint32_t)y * 0x165667B19E3779F9ull;
+  h += (uint64_t)(uint32_t)z * 0x27D4EB2F165667C5ull;
+  // 64-bit finaliser (MurmurHash3 fmix64)
+  h ^= h >> 33;
+  h *= 0xFF51AFD7ED558CCDull;
+  h ^= h >> 33;
+  h *= 0xC4CEB9FE1A85EC53ull;
+  h ^= h >> 33;
+  return (uint32_t)h;
+}
+
+__device__ __forceinline__ bool same(int4 a, int b, int x, int y, int z) {
+  return a.x == b && a.y == x && a.z == y && a.w == z;
+}
+
+__global__ void kmap_insert_kernel(const int4* __restrict__ coords, int64_t n, int32_t* table,
+                                   uint32_t mask, int32_t* status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = __ldg(&coords[i]);
+  uint32_t h = hash_coord(c.x, c.y, c.z, c.w) & mask;
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    int32_t cur = *((volatile int32_t*)&table[h]);
+    if (cur < 0) {
+      const int32_t prev = atomicCAS(&table[h], -1, (int32_t)i);
+      if (prev < 0) return;  // claimed an empty slot
+      cur = prev;
+    }
+    // A slot's key never changes once claimed: it only moves to larger rows of the same key.
+    if (same(__ldg(&coords[cur]), c.x, c.y, c.z, c.w)) {
+      atomicMax(&table[h], (int32_t)i);
+      return;
+    }
+    h = (h + 1) & mask;
+  }
+  report(status, SV_DEVICE_TABLE_FULL);
+}
+
+__device__ __forceinline__ int32_t kmap_lookup(const int4* __restrict__ coords,
+                                               const int32_t* __restrict__ table, uint32_t mask,
+                                               int b, int x, int y, int z) {
+  uint32_t h = hash_coord(b, x, y, z) & mask;
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    const int32_t cur = __ldg(&table[h]);
+    if (cur < 0) return -1;
+    if (same(__ldg(&coords[cur]), b, x, y, z)) return cur;
+    h = (h + 1) & mask;
+  }
+  return -1;
+}
+
+// One thread per (row, offset): writes nbr row-major, so consecutive threads store
+// consecutive words.
+__global__ void kmap_probe_kernel(const int4* __restrict__ coords, int64_t n,
+                                  const int32_t* __restrict__ table, uint32_t mask, int k0,
+                                  int k1, int k2, int d0, int d1, int d2,
+                                  int32_t* __restrict__ nbr) {
+  const int kvol = k0 * k1 * k2;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * kvol) return;
+  const int64_t p = idx / kvol;
+  const int k = (int)(idx - p * kvol);
+  const int c = k % k2;
+  const int b = (k / k2) % k1;
+  const int a = k / (k1 * k2);
+  const int4 q = __ldg(&coords[p]);
+  const int64_t x = (int64_t)q.y + (int64_t)(a - k0 / 2) * d0;
+  const int64_t y = (int64_t)q.z + (int64_t)(b - k1 / 2) * d1;
+  const int64_t z = (int64_t)q.w + (int64_t)(c - k2 / 2) * d2;
+  int32_t r = -1;
+  if (x >= INT32_MIN && x <= INT32_MAX && y >= INT32_MIN && y <= INT32_MAX && z >= INT32_MIN &&
+      z <= INT32_MAX)
+    r = kmap_lookup(coords, table, mask, q.x, (int)x, (int)y, (int)z);
+  nbr[idx] = r;
+}
+
+__global__ void row_mask_kernel(const int32_t* __restrict__ nbr, int64_t n, int kvol,
+                                uint32_t* __restrict__ masks, int32_t* __restrict__ rows) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n) return;
+  uint32_t m = 0;
+  for (int k = 0; k < kvol; ++k) m |= (uint32_t)(__ldg(&nbr[p * kvol + k]) >= 0) << k;
+  masks[p] = m;
+  rows[p] = (int32_t)p;
+}
+
+size_t plan_cub_bytes(int64_t n) {
+  size_t bytes = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                  (const int32_t*)nullptr, (int32_t*)nullptr, (int)n, 0, 32);
+  return bytes;
+}
+
+}  // namespace
+}  // namespace sv
+
+using namespace sv;
+
+extern "C" int64_t sv_kmap_table_slots(int64_t n) {
+  int64_t slots = 64;
+  while (slots < 2 * n) slots <<= 1;
+  return slots;
+}
+
+extern "C" size_t sv_kmap_workspace_bytes(int64_t table_slots) {
+  return table_slots > 0 ? (size_t)table_slots * sizeof(int32_t) : 0;
+}
+
+extern "C" int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                             const int32_t dilation[3], int32_t* nbr, int64_t table_slots,
+                             void* workspace, size_t workspace_bytes, int32_t* status,
+                             sv_stream_t stream) {
+  if (n < 0 || kernel == nullptr || dilation == nullptr)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_kmap_build: bad arguments");
+  for (int i = 0; i < 3; ++i)
+    if (kernel[i] <= 0 || kernel[i] % 2 == 0)
+      SV_FAIL(SV_ERR_BAD_SHAPE, "sparse submanifold kernels must have three odd dimensions");
+  const int64_t kvol = (int64_t)kernel[0] * kernel[1] * kernel[2];
+  if (n == 0) return SV_OK;
+  if (coords == nullptr || nbr == nullptr)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_kmap_build: null coords or nbr");
+  if (n > INT32_MAX - 1) SV_FAIL(SV_ERR_UNSUPPORTED, "sv_kmap_build: more than 2^31-2 rows");
+  if (!aligned16(coords)) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "coords must be 16-byte aligned");
+  if (table_slots < 64 || (table_slots & (table_slots - 1)) != 0 || table_slots > (1ll << 31))
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "table_slots must be a power of two in [64, 2^31]");
+  if (workspace == nullptr || workspace_bytes < sv_kmap_workspace_bytes(table_slots))
+    SV_FAIL(SV_ERR_WORKSPACE, "sv_kmap_build: workspace too small");
+  cudaStream_t s = to_stream(stream);
+  int32_t* table = static_cast<int32_t*>(workspace);
+  const uint32_t mask = (uint32_t)(table_slots - 1);
+  SV_CUDA_TRY(cudaMemsetAsync(table, 0xFF, (size_t)table_slots * sizeof(int32_t), s));
+  const int threads = 256;
+  kmap_insert_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, s>>>(
+      reinterpret_cast<const int4*>(coords), n, table, mask, status);
+  SV_LAUNCH_CHECK();
+  const int64_t total = n * kvol;
+  kmap_probe_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, s>>>(
+      reinterpret_cast<const int4*>(coords), n, table, mask, kernel[0], kernel[1], kernel[2],
+      dilation[0], dilation[1], dilation[2], nbr);
+  SV_LAUNCH_CHECK();
+  return SV_OK;
+}
+
+extern "C" size_t sv_conv_plan_workspace_bytes(int64_t n) {
+  if (n <= 0) return 0;
+  return align_up((size_t)n * 4, 256) * 3 + align_up(plan_cub_bytes(n), 256);
+}
+
+extern "C" int sv_conv_plan(const int32_t* nbr, int64_t n, int kvol, int32_t* row_order,
+                            void* workspace, size_t workspace_bytes, sv_stream_t stream) {
+  if (n < 0 || kvol <= 0) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv_plan: bad sizes");
+  if (kvol > 32) SV_FAIL(SV_ERR_UNSUPPORTED, "sv_conv_plan: kernel volume above 32");
+  if (n == 0) return SV_OK;
+  if (n > INT32_MAX) SV_FAIL(SV_ERR_UNSUPPORTED, "sv_conv_plan: more than 2^31-1 rows");
+  if (nbr == nullptr || row_order == nullptr)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv_plan: null pointer");
+  if (workspace == nullptr || workspace_bytes < sv_conv_plan_workspace_bytes(n))
+    SV_FAIL(SV_ERR_WORKSPACE, "sv_conv_plan: workspace too small");
+  cudaStream_t s = to_stream(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t vec = align_up((size_t)n * 4, 256);
+  uint32_t* masks = reinterpret_cast<uint32_t*>(ws);
+  uint32_t* masks_sorted = reinterpret_cast<uint32_t*>(ws + vec);
+  int32_t* rows = reinterpret_cast<int32_t*>(ws + 2 * vec);
+  void* cub_tmp = ws + 3 * vec;
+  size_t cub_bytes = workspace_bytes - 3 * vec;
+  row_mask_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(nbr, n, kvol, masks, rows);
+  SV_LAUNCH_CHECK();
+  SV_CUDA_TRY(cub::DeviceRadixSort::SortPairs(cub_tmp, cub_bytes, masks, masks_sorted, rows,
+                                              row_order, (int)n, 0, kvol, s));
+  return SV_OK;
+}

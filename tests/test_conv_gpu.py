@@ -1,0 +1,205 @@
+"""Sparse convolution on the GPU against the reference's fallback (fp32 oracle).
+
+Tolerances, from the path's contract:
+* fp32 features: within rtol 1e-4 of the fp32 reference (plus an absolute floor of
+  1e-4 x max|ref| for outputs near zero);
+* fp16 / bf16 features: max relative error <= 1e-2 of the fp32 reference, where
+  max relative error = max|out - ref| / max|ref| and the reference is computed in fp32 from
+  the same (rounded) inputs.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from mlx_diffuser_b200 import _native as N
+from mlx_diffuser_b200 import scenes
+from mlx_diffuser_b200.kernels.sparse import conv3d_forward, sparse_conv3d
+from mlx_diffuser_b200.layers.sparse import (
+    SparseConv3D,
+    SparseTensor,
+    build_neighbor_map,
+    conv_row_order,
+)
+from oracle import sparse_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+HALF_TOL = 1e-2
+F32_RTOL = 1e-4
+
+
+def max_rel_err(got, ref) -> float:
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = max(np.abs(ref).max(), 1e-30)
+    return float(np.abs(got - ref).max() / scale)
+
+
+def assert_f32_close(got, ref):
+    ref = np.asarray(ref, np.float64)
+    np.testing.assert_allclose(got, ref, rtol=F32_RTOL, atol=F32_RTOL * max(np.abs(ref).max(), 1e-6))
+
+
+def _module(weight, bias, dtype, dilation=1, algo=N.SV_CONV_AUTO):
+    o, k, _, _, i = weight.shape
+    conv = SparseConv3D(i, o, k, dilation=dilation).to(DEV)
+    conv.conv.weight = torch.from_numpy(weight).to(DEV, dtype)
+    conv.conv.bias = torch.from_numpy(bias).to(DEV, dtype)
+    conv.algo = algo
+    return conv
+
+
+def _run(coords, feats, weight, bias, dtype, dilation=1, algo=N.SV_CONV_AUTO):
+    conv = _module(weight, bias, dtype, dilation, algo)
+    x = SparseTensor(torch.from_numpy(feats).to(DEV, dtype), torch.from_numpy(coords).to(DEV))
+    out = conv(x).features.float().cpu().numpy()
+    N.check_device_status(DEV)
+    return out, x
+
+
+def _rounded(a, dtype):
+    return torch.from_numpy(np.asarray(a, np.float32)).to(dtype).float().numpy()
+
+
+def test_conv_fp32_matches_golden(golden):
+    _, g = golden
+    out, _ = _run(g["coords"], g["features"], g["weight"], g["bias"], torch.float32,
+                  int(g["dilation"]))
+    assert_f32_close(out, g["conv_out"])
+
+
+def test_reference_metal_kernel_equals_fallback_four_points():
+    """``tests/test_trellis.py:119-131`` of the reference, against its recorded output."""
+
+    from tests.conftest import load_golden
+
+    g = load_golden("ref_test_four_points")
+    out, _ = _run(g["coords"], g["features"], g["weight"], g["bias"], torch.float32)
+    np.testing.assert_allclose(out, g["conv_out"], atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("algo", [N.SV_CONV_AUTO, N.SV_CONV_SIMT])
+def test_conv_half_matches_fp32_reference(golden, dtype, algo):
+    _, g = golden
+    f = _rounded(g["features"], dtype)
+    w = _rounded(g["weight"], dtype)
+    b = _rounded(g["bias"], dtype)
+    ref = O.sparse_conv3d(f, g["nbr"], O.spconv_weight_to_kio(w), b)
+    out, _ = _run(g["coords"], f, w, b, dtype, int(g["dilation"]), algo)
+    assert max_rel_err(out, ref) <= HALF_TOL
+
+
+@pytest.mark.parametrize(
+    "cin,cout",
+    [(64, 32), (64, 64), (128, 128), (64, 256), (192, 512), (1024, 1024), (256, 96)],
+)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tcgen05_shapes(cin, cout, dtype):
+    coords = scenes.batched(
+        [scenes.shell(16, 5.5, 2.0, 1.0, seed=7), scenes.shell(12, 4.0, 2.0, 0.5, seed=9)]
+    )
+    f = _rounded(scenes.normal_features(len(coords), cin, seed=1), dtype)
+    w = _rounded(scenes.conv_weight(cout, cin, 3, seed=2), dtype)
+    b = _rounded(np.random.default_rng(3).standard_normal(cout).astype(np.float32) * 0.1, dtype)
+    nbr = O.build_neighbor_map(coords, 3)
+    ref = O.sparse_conv3d(f, nbr, O.spconv_weight_to_kio(w), b)
+    out, _ = _run(coords, f, w, b, dtype, algo=N.SV_CONV_TCGEN05)
+    assert max_rel_err(out, ref) <= HALF_TOL
+
+
+def test_tcgen05_agrees_with_simt_and_ignores_row_order():
+    coords = scenes.shell32_batch(2)
+    cin = cout = 128
+    dtype = torch.bfloat16
+    feats = torch.from_numpy(scenes.normal_features(len(coords), cin, seed=5)).to(DEV, dtype)
+    w = torch.from_numpy(scenes.conv_weight(cout, cin, 3, seed=6)).to(DEV, dtype).contiguous()
+    b = torch.zeros(cout, device=DEV, dtype=dtype)
+    nbr = build_neighbor_map(torch.from_numpy(coords).to(DEV), 3)
+    order = conv_row_order(nbr)
+    tc_plain = conv3d_forward(feats, nbr, w, N.SV_WEIGHT_OKI, b, cout, algo=N.SV_CONV_TCGEN05)
+    tc_order = conv3d_forward(feats, nbr, w, N.SV_WEIGHT_OKI, b, cout, row_order=order,
+                              algo=N.SV_CONV_TCGEN05)
+    simt = conv3d_forward(feats, nbr, w, N.SV_WEIGHT_OKI, b, cout, row_order=order,
+                          algo=N.SV_CONV_SIMT)
+    N.check_device_status(DEV)
+    assert max_rel_err(tc_plain.float().cpu(), tc_order.float().cpu()) <= 1e-6
+    assert max_rel_err(tc_order.float().cpu(), simt.float().cpu()) <= HALF_TOL
+
+
+def test_functional_kio_matches_module_oki():
+    coords = scenes.shell(16, 5.5, 2.0, 1.0, seed=11)
+    for dtype, cin, cout in ((torch.bfloat16, 64, 64), (torch.float32, 16, 24)):
+        f = scenes.normal_features(len(coords), cin, seed=12)
+        w = scenes.conv_weight(cout, cin, 3, seed=13)
+        b = np.random.default_rng(14).standard_normal(cout).astype(np.float32)
+        mod, x = _run(coords, f, w, b, dtype)
+        nbr = x.cache["neighbors_3_1_(1, 1, 1)"]
+        fun = sparse_conv3d(
+            x.features, nbr, torch.from_numpy(O.spconv_weight_to_kio(w)).to(DEV, dtype),
+            torch.from_numpy(b).to(DEV, dtype),
+        )
+        assert fun.dtype == dtype
+        assert max_rel_err(fun.float().cpu(), mod) <= (1e-6 if dtype == torch.float32 else 1e-2)
+
+
+def test_config2_full_size_sampled_rows():
+    """4 x ~6k-voxel shells at 32^3, 1024 -> 1024, bf16: 384 sampled rows against fp32."""
+
+    coords = scenes.shell32_batch(4)
+    dtype = torch.bfloat16
+    f = _rounded(scenes.normal_features(len(coords), 1024, seed=21), dtype)
+    w = _rounded(scenes.conv_weight(1024, 1024, 3, seed=22), dtype)
+    b = np.zeros(1024, np.float32)
+    out, x = _run(coords, f, w, b, dtype)
+    nbr = x.cache["neighbors_3_1_(1, 1, 1)"].cpu().numpy()
+    assert np.array_equal(nbr, O.build_neighbor_map(coords, 3))
+    rows = np.random.default_rng(0).choice(len(coords), 384, replace=False)
+    wk = O.spconv_weight_to_kio(w)
+    ref = np.zeros((len(rows), 1024), np.float32)
+    for k in range(27):
+        idx = nbr[rows, k]
+        ok = idx >= 0
+        ref[ok] += f[idx[ok]] @ wk[k]
+    assert max_rel_err(out[rows], ref) <= HALF_TOL
+
+
+def test_conv_edge_cases():
+    dtype = torch.bfloat16
+    cin = cout = 64
+    w = torch.from_numpy(scenes.conv_weight(cout, cin, 3, seed=1)).to(DEV, dtype).contiguous()
+    bias = torch.linspace(-1, 1, cout, device=DEV).to(dtype)
+    for algo in (N.SV_CONV_TCGEN05, N.SV_CONV_SIMT):
+        # all neighbours missing -> bias only
+        feats = torch.randn(5, cin, device=DEV).to(dtype)
+        nbr = torch.full((5, 27), -1, dtype=torch.int32, device=DEV)
+        out = conv3d_forward(feats, nbr, w, N.SV_WEIGHT_OKI, bias, cout, algo=algo)
+        assert torch.equal(out, bias.expand(5, cout))
+        # out-of-range neighbour indices are flagged and treated as missing
+        nbr[:, 0] = 99
+        out = conv3d_forward(feats, nbr, w, N.SV_WEIGHT_OKI, bias, cout, algo=algo)
+        assert torch.equal(out, bias.expand(5, cout))
+        with pytest.raises(RuntimeError, match="out of range"):
+            N.check_device_status(DEV)
+    # partial tiles: N = 1, 127, 129, 257
+    for n in (1, 127, 129, 257):
+        coords = scenes.shell(16, 5.5, 2.0, 1.0, seed=3)[:n]
+        f = _rounded(scenes.normal_features(n, cin, seed=n), dtype)
+        wn = _rounded(scenes.conv_weight(cout, cin, 3, seed=4), dtype)
+        out, _ = _run(coords, f, wn, np.zeros(cout, np.float32), dtype)
+        ref = O.sparse_conv3d(f, O.build_neighbor_map(coords, 3), O.spconv_weight_to_kio(wn),
+                              np.zeros(cout, np.float32))
+        assert max_rel_err(out, ref) <= HALF_TOL
+    # empty input and zero output channels
+    empty = SparseTensor(torch.zeros((0, cin), device=DEV, dtype=dtype),
+                         torch.zeros((0, 4), dtype=torch.int32, device=DEV))
+    conv = SparseConv3D(cin, cout).to(DEV)
+    conv.cast_dtype(dtype)
+    assert conv(empty).features.shape == (0, cout)
+    zero_out = sparse_conv3d(torch.zeros((3, cin), device=DEV), torch.zeros((3, 27), dtype=torch.int32),
+                             torch.zeros((27, cin, 0)), torch.zeros(0))
+    assert zero_out.shape == (3, 0)

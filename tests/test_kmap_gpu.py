@@ -1,0 +1,111 @@
+"""Kernel map on the GPU: bit-exact against the reference's build_neighbor_map.
+
+Golden fixtures come from the reference's own code; full-size scenes are checked against the
+oracle (itself pinned to the fixtures in test_oracle.py).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from mlx_diffuser_b200 import _native as N
+from mlx_diffuser_b200 import scenes
+from mlx_diffuser_b200.layers.sparse import build_neighbor_map, conv_row_order
+from oracle import sparse_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda", 0)
+
+
+def _gpu_map(coords, ks=3, dl=1, **kw):
+    out = build_neighbor_map(torch.from_numpy(np.ascontiguousarray(coords)).to(DEV), ks, dl, **kw)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_kmap_matches_golden(golden):
+    _, g = golden
+    assert np.array_equal(_gpu_map(g["coords"], int(g["kernel_size"]), int(g["dilation"])), g["nbr"])
+    i = 0
+    while f"nbr_extra{i}" in g:
+        ks = tuple(int(v) for v in g[f"nbr_extra{i}_kernel"])
+        dl = tuple(int(v) for v in g[f"nbr_extra{i}_dilation"])
+        assert np.array_equal(_gpu_map(g["coords"], ks, dl), g[f"nbr_extra{i}"])
+        i += 1
+
+
+@pytest.mark.parametrize(
+    "name",
+    ["shell64", "shell32x4", "scene128", "uniform64_30pct", "uniform128_2pct_b16"],
+)
+def test_kmap_full_size_matches_oracle(name):
+    coords = {
+        "shell64": lambda: scenes.shell64(0),
+        "shell32x4": lambda: scenes.shell32_batch(4),
+        "scene128": lambda: scenes.scene128(0),
+        "uniform64_30pct": lambda: scenes.uniform(64, 0.30, 5),
+        "uniform128_2pct_b16": lambda: scenes.batched(
+            [scenes.uniform(128, 0.02, 100 + b) for b in range(16)]
+        ),
+    }[name]()
+    want = O.build_neighbor_map(coords, 3)
+    got = _gpu_map(coords)
+    assert np.array_equal(got, want)
+
+
+def test_kmap_edge_cases_match_dict_oracle():
+    imax, imin = np.iinfo(np.int32).max, np.iinfo(np.int32).min
+    c = np.array(
+        [
+            [0, imax, 0, 0],
+            [0, imax - 1, 0, 0],
+            [0, imin, imin, imin],
+            [0, imin + 1, imin, imin],
+            [-3, 5, 5, 5],     # negative batch index is just another key
+            [-3, 5, 6, 5],
+            [7, 0, 0, 0],
+            [7, 0, 0, 0],      # duplicate rows: the later row wins
+            [7, 0, 0, 1],
+            [7, 0, 0, 0],
+        ],
+        np.int32,
+    )
+    for ks, dl in ((3, 1), ((3, 1, 5), (2, 1, 1)), (1, 1), (5, 3)):
+        want = O.build_neighbor_map_dict(c, ks, dl)
+        assert np.array_equal(_gpu_map(c, ks, dl), want), (ks, dl)
+    m = _gpu_map(c)
+    assert m[7, 13] == 9 and m[9, 13] == 9
+
+
+def test_kmap_empty_and_single():
+    assert _gpu_map(np.zeros((0, 4), np.int32)).shape == (0, 27)
+    single = _gpu_map(np.array([[0, 3, 4, 5]], np.int32))
+    assert single[0, 13] == 0 and (np.delete(single[0], 13) == -1).all()
+
+
+def test_kmap_undersized_table_raises():
+    coords = scenes.shell(16, 5.5, 2.0, 1.0, seed=3)
+    assert len(coords) > 64
+    with pytest.raises(RuntimeError, match="hash table full"):
+        _gpu_map(coords, table_slots=64)
+    # a correctly sized explicit table works and leaves the status clean
+    assert np.array_equal(_gpu_map(coords, table_slots=4096), O.build_neighbor_map(coords, 3))
+
+
+def test_conv_row_order_groups_rows_by_mask():
+    coords = scenes.shell32_batch(2)
+    nbr = build_neighbor_map(torch.from_numpy(coords).to(DEV), 3)
+    order = conv_row_order(nbr).cpu().numpy()
+    n = len(coords)
+    assert np.array_equal(np.sort(order), np.arange(n))
+    host = nbr.cpu().numpy()
+    masks = ((host >= 0).astype(np.int64) << np.arange(27)).sum(1)
+    m = masks[order]
+    assert (np.diff(m) >= 0).all()
+    same = np.diff(m) == 0
+    assert (np.diff(order)[same] > 0).all()  # stable: spatial order kept inside a group
+    assert conv_row_order(build_neighbor_map(torch.from_numpy(coords).to(DEV), 5)) is None
+    N.check_device_status(DEV)
