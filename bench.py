@@ -1,0 +1,460 @@
+#!/usr/bin/env python
+"""Benchmark of the TRELLIS sparse-voxel hot path on B200: submanifold 3x3x3 sparse conv3d,
+active voxels per second.
+
+Workload (per GPU): 4 noisy-sphere shells on a 32^3 grid (about 6k voxels each, 24k total),
+Cin = Cout = 1024, bf16 features and weights, fp32 accumulation. One step = what a user's
+``SparseConv3D(1024, 1024)(SparseTensor(feats, coords))`` does on a fresh tensor: build the
+kernel map (hash insert + 27-offset probe) and the row schedule, then the tensor-core conv.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 it runs under torchrun, one rank per GPU; each rank convolves its own batch of 4
+shells (weak scaling, no communication on the data path) and rank 0 prints the JSON line.
+``--impl reference`` times the reference's own algorithm (dict-based neighbour map and the
+gather-matmul fallback, restated in NumPy) on the host cores, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+CIN = COUT = 1024
+SHELLS_PER_GPU = 4
+METRIC = "sparse conv3d active-voxels/s"
+UNIT = "voxels/s"
+WORKLOAD = "shell32x4_conv1024_bf16"
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "conv_tc_shell32x4_c1024_bf16.md")
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    return p.parse_args()
+
+
+def rank_inputs(rank: int):
+    from mlx_diffuser_b200 import scenes
+
+    coords = scenes.shell32_batch(SHELLS_PER_GPU, seed=SHELLS_PER_GPU * rank)
+    feats = scenes.normal_features(len(coords), CIN, seed=1000 + rank)
+    weight = scenes.conv_weight(COUT, CIN, 3, seed=7)
+    return coords, feats, weight
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profiled_traffic() -> float | None:
+    """DRAM bytes per conv launch from the committed ncu summary, if one exists."""
+
+    if not os.path.exists(PROFILE_SUMMARY):
+        return None
+    with open(PROFILE_SUMMARY) as f:
+        for line in f:
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    return None
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline: the reference's algorithm on the host cores
+# ---------------------------------------------------------------------------------------------
+
+
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        counts = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if counts:
+            return int(max(counts))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_sample(rank: int = 0):
+    """One bounded sample of the workload: the first of the rank's shells (about 6k voxels)."""
+
+    coords, feats, weight = rank_inputs(rank)
+    first = coords[:, 0] == 0
+    return coords[first], feats[first], weight
+
+
+def cpu_step(coords, feats, weight_kio, bias) -> None:
+    from oracle import sparse_oracle as O
+
+    nbr = O.build_neighbor_map_dict(coords, 3)
+    O.sparse_conv3d_fallback_literal(feats, nbr, weight_kio, bias)
+
+
+def cpu_baseline(reps: int = 2) -> dict:
+    from oracle import sparse_oracle as O
+
+    coords, feats, weight = cpu_sample(0)
+    wk = O.spconv_weight_to_kio(weight)
+    bias = np.zeros(COUT, np.float32)
+    cpu_step(coords, feats, wk, bias)  # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        cpu_step(coords, feats, wk, bias)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {
+        "value": len(coords) / t,
+        "unit": UNIT,
+        "cores": blas_threads(),
+        "kind": "port",
+        "sample": (
+            f"1 of 4 shells ({len(coords)} voxels): dict neighbour map + the reference's "
+            f"gather-matmul fallback in fp32 NumPy, median of {reps}"
+        ),
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import sparse_oracle as O
+
+    coords, feats, weight = cpu_sample(0)
+    wk = O.spconv_weight_to_kio(weight)
+    bias = np.zeros(COUT, np.float32)
+    for _ in range(args.warmup):
+        cpu_step(coords, feats, wk, bias)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(coords, feats, wk, bias)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = len(coords) / dt
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {
+            "workload": WORKLOAD,
+            "sample": f"1 of 4 shells per step ({len(coords)} voxels), host cores",
+        },
+        "cpu_baseline": {
+            "value": value,
+            "unit": UNIT,
+            "cores": blas_threads(),
+            "kind": "port",
+            "sample": (
+                f"1 of 4 shells ({len(coords)} voxels) per step: dict neighbour map + the "
+                "reference's gather-matmul fallback in fp32 NumPy"
+            ),
+        },
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------------
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples taken while the timed region runs."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+        "clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=self.file, stderr=subprocess.DEVNULL,
+            )
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in self.file.read().strip().splitlines():
+            cols = [c.strip() for c in row.split(",")]
+            if len(cols) < 8:
+                continue
+            try:
+                sm.append(float(cols[1]))
+                mx.append(float(cols[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, cols[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        if not sm:
+            return None
+        return {
+            "sm_mhz": statistics.median(sm),
+            "sm_max_mhz": max(mx),
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+def count_launches(step_fn) -> int | None:
+    """Kernels one step launches, counted by the CUDA profiler on an extra untimed step."""
+
+    try:
+        import torch
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step_fn()
+            torch.cuda.synchronize()
+        kernels = [
+            e for e in prof.events()
+            if e.device_type == torch.autograd.DeviceType.CUDA and "memset" not in e.name.lower()
+            and "memcpy" not in e.name.lower()
+        ]
+        return len(kernels) or None
+    except Exception:
+        return None
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from mlx_diffuser_b200 import _native as N
+    from mlx_diffuser_b200.layers.sparse import (
+        SparseConv3D,
+        SparseTensor,
+        build_neighbor_map,
+        conv_row_order,
+    )
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    coords_np, feats_np, weight_np = rank_inputs(rank)
+    n = len(coords_np)
+    coords = torch.from_numpy(coords_np).to(dev)
+    feats = torch.from_numpy(feats_np).to(dev, torch.bfloat16)
+    conv = SparseConv3D(CIN, COUT, 3).to(dev)
+    conv.conv.weight = torch.from_numpy(weight_np).to(dev, torch.bfloat16).contiguous()
+    conv.conv.bias = torch.zeros(COUT, device=dev, dtype=torch.bfloat16)
+    spatial = (32, 32, 32)
+    key = "neighbors_3_1_(1, 1, 1)"
+    plan_key = "conv_rows_3_1_(1, 1, 1)"
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        x = SparseTensor(feats, coords, SHELLS_PER_GPU, spatial)
+        nbr = build_neighbor_map(x.coords, 3)
+        x.cache[key] = nbr
+        x.cache[plan_key] = conv_row_order(nbr)
+        mid.record()
+        return conv(x)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    mid = torch.cuda.Event(enable_timing=True)
+    for _ in range(args.warmup):
+        step()
+    y = step()
+    torch.cuda.synchronize()
+    N.check_device_status(dev)
+    nbr = build_neighbor_map(coords, 3)
+    pairs = int((nbr >= 0).sum().item())
+
+    events = [
+        (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+         torch.cuda.Event(enable_timing=True))
+        for _ in range(args.steps)
+    ]
+    sampler = ClockSampler(local)
+    barrier()
+    sampler.start()
+    for a, b, c in events:
+        flush.fill_(1.0)
+        a.record()
+        mid = b
+        step()
+        c.record()
+    barrier()
+    clocks = sampler.stop()
+    step_ms = [a.elapsed_time(c) for a, _, c in events]
+    conv_ms = [b.elapsed_time(c) for _, b, c in events]
+    kmap_ms = [a.elapsed_time(b) for a, b, _ in events]
+    mean_step = sum(step_ms) / len(step_ms)
+    mean_conv = sum(conv_ms) / len(conv_ms)
+
+    # ---- end to end through the public API, host buffers in and out ----
+    coords_h = torch.from_numpy(coords_np).pin_memory()
+    feats_h = torch.from_numpy(feats_np).to(torch.bfloat16).pin_memory()
+    out_h = torch.empty((n, COUT), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        c_d = coords_h.to(dev, non_blocking=True)
+        f_d = feats_h.to(dev, non_blocking=True)
+        out = conv(SparseTensor(f_d, c_d, SHELLS_PER_GPU, spatial)).features
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(max(args.warmup, 1)):
+        e2e_step()
+    e2e_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+    barrier()
+    for a, c in e2e_events:
+        flush.fill_(1.0)
+        a.record()
+        e2e_step()
+        c.record()
+    barrier()
+    mean_e2e = sum(a.elapsed_time(c) for a, c in e2e_events) / args.steps
+    ref_out = y.features.float()
+    assert torch.allclose(out_h.to(dev).float(), ref_out), "e2e output differs from device run"
+
+    def mid_step():
+        nonlocal mid
+        mid = torch.cuda.Event(enable_timing=True)
+        step()
+
+    launches = count_launches(mid_step)
+
+    stats = torch.tensor([mean_step, mean_conv, mean_e2e, float(n), float(pairs)],
+                         dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = stats[:3].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tot = stats[3:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        stats = torch.cat([tmax, tot])
+    mean_step, mean_conv, mean_e2e, voxels, total_pairs = (float(v) for v in stats.cpu())
+
+    if rank == 0:
+        peaks = measured_peaks()
+        flops = 2.0 * CIN * COUT * pairs  # rank 0's launch (ranks are identical in shape)
+        achieved = flops / (statistics.mean(conv_ms) * 1e-3) / 1e12
+        traffic = profiled_traffic()
+        line = {
+            "metric": METRIC,
+            "value": voxels / (mean_step * 1e-3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": mean_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": WORKLOAD,
+                "description": (
+                    "4 seeded noisy-sphere shells on 32^3 per GPU, submanifold 3x3x3 conv "
+                    "1024->1024 bf16, fp32 accumulate; each step builds the kernel map"
+                ),
+                "voxels_per_gpu": n,
+                "valid_pairs_per_gpu": pairs,
+                "kmap_ms": statistics.mean(kmap_ms),
+                "conv_ms": statistics.mean(conv_ms),
+                "l2": "flushed between steps (256 MiB write outside the timed events)",
+                "parallelism": f"batch-shard x{world}",
+            },
+            "roofline": {
+                "bound": "tensor",
+                "kernel": "conv_tc_kernel<256, bf16>",
+                "achieved": achieved,
+                "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"],
+                "peak_source": peaks["source"] + " (burst)",
+                "flops_per_launch": flops,
+                "traffic": traffic,
+            },
+            "e2e": {
+                "value": voxels / (mean_e2e * 1e-3),
+                "unit": UNIT,
+                "h2d_bytes_per_step": int(coords_h.numel() * 4 + feats_h.numel() * 2),
+                "d2h_bytes_per_step": int(out_h.numel() * 2),
+            },
+            "gpu_launches": None if launches is None else launches * args.steps,
+            "clocks": clocks,
+        }
+        if world == 1:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

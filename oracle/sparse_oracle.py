@@ -225,3 +225,24 @@ def valid_pairs(neighbors) -> int:
     """P: the number of valid (output, input, offset) triples in a kernel map."""
 
     return int((np.asarray(neighbors) >= 0).sum())
+
+
+def sparse_conv3d_fallback_literal(features, neighbors, weights, bias) -> np.ndarray:
+    """Operation-for-operation copy of the reference's fallback loop
+    (``src/mlx_diffuser/kernels/sparse.py:47-55``) in NumPy float32: every offset gathers all
+    N rows through ``max(index, 0)``, multiplies by W[k] and masks the invalid rows. Same result
+    as :func:`sparse_conv3d`, same amount of work as the reference; the CPU baseline times it."""
+
+    f = np.asarray(features, np.float32)
+    nbr = np.asarray(neighbors, np.int32)
+    w = np.asarray(weights, np.float32)
+    b = np.asarray(bias, np.float32)
+    points, kernel_volume = nbr.shape
+    out = np.broadcast_to(b, (points, b.shape[0]))
+    for k in range(kernel_volume):
+        index = nbr[:, k]
+        valid = index >= 0
+        safe_index = np.maximum(index, 0)
+        contribution = f[safe_index] @ w[k]
+        out = out + contribution * valid[:, None]
+    return out
