@@ -362,7 +362,7 @@ def sparse_downsample(x: SparseTensor, factor: int = 2) -> SparseTensor:
     m = int(m_out.value)
     feats = x.features
     trailing = feats.shape[1:]
-    flat = feats.reshape(n, -1).contiguous()
+    flat = feats.reshape(n, math.prod(trailing)).contiguous()
     if flat.dtype not in N.DTYPE_CODE:
         flat = flat.to(torch.float32)
     pooled = torch.empty((m, flat.shape[1]), dtype=flat.dtype, device=dev)
@@ -398,7 +398,7 @@ def sparse_upsample(x: SparseTensor, factor: int = 2) -> SparseTensor:
     N.require_cuda(feats, "features")
     m = feats.shape[0]
     n = inverse.shape[0]
-    flat = feats.reshape(m, -1).contiguous()
+    flat = feats.reshape(m, math.prod(feats.shape[1:])).contiguous()
     out = torch.empty((n, flat.shape[1]), dtype=flat.dtype, device=flat.device)
     # the gather copies rows of bytes: describe any row as float32 / 16-bit words
     row_bytes = flat.shape[1] * flat.element_size()
