@@ -87,6 +87,23 @@ SV_API int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t kernel[
                          void* workspace, size_t workspace_bytes, int32_t* status,
                          sv_stream_t stream);
 
+/* Allocation-free kernel map. No counterpart in mlx_diffuser: it exists for callers that
+ * cannot allocate device memory -- e.g. a host program that keeps all GPU memory to itself and
+ * does not let plugins call cudaMalloc, or a caller from another language that has only its
+ * input and output buffers and no device allocator. Same result as sv_kmap_build, but the hash
+ * table is a fixed array inside this library (4 MiB per GPU that loads the library, held until
+ * the process exits) instead of caller workspace; nothing is allocated.
+ * Limits and rules:
+ *  - n <= SV_KMAP_STATIC_MAX_ROWS, otherwise SV_ERR_UNSUPPORTED (with a message) and no work;
+ *  - the first call on a device looks up the array's device address (cudaGetSymbolAddress), so
+ *    make that first call before any stream capture;
+ *  - all calls on a device share the one table: calls that overlap on the GPU race. Each call
+ *    clears the slots it uses before inserting, so back-to-back calls are independent. */
+#define SV_KMAP_STATIC_MAX_ROWS 524288
+SV_API int sv_kmap_build_static(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                                const int32_t dilation[3], int32_t* nbr, int32_t* status,
+                                sv_stream_t stream);
+
 /* Row schedule for the tensor-core convolution: a permutation of 0..n-1 that groups rows with
  * equal neighbour-validity masks (stable, so rows with one mask keep their spatial order).
  * Needs kvol <= 32. Workspace: sv_conv_plan_workspace_bytes(n). */

@@ -9,6 +9,9 @@
 //    atomicMax on the slot: the largest row index among equal rows wins;
 //  * offsets are enumerated in the reference's order (:160-169); a neighbour coordinate that
 //    leaves the int32 range simply misses, as a Python dict lookup of that tuple would.
+#include <mutex>
+#include <string>
+
 #include <cub/device/device_radix_sort.cuh>
 
 #include "common.cuh"
@@ -190,4 +193,58 @@ extern "C" int sv_conv_plan(const int32_t* nbr, int64_t n, int kvol, int32_t* ro
   SV_CUDA_TRY(cub::DeviceRadixSort::SortPairs(cub_tmp, cub_bytes, masks, masks_sorted, rows,
                                               row_order, (int)n, 0, kvol, s));
   return SV_OK;
+}
+
+// ---- allocation-free kernel map ------------------------------------------------------------
+//
+// For callers that cannot allocate device memory themselves -- a host application that owns
+// every byte of GPU memory and forbids plugins from calling cudaMalloc, or a foreign-language
+// caller that holds only its input and output buffers and no device allocator -- the hash
+// table of sv_kmap_build lives here, in a fixed array compiled into the library. Every GPU that
+// loads the library holds this array (SV_KMAP_STATIC_MAX_ROWS rows' worth of slots, 4 MiB)
+// until the process exits. All calls on a device share it, so calls whose work overlaps on the
+// GPU (different streams, or different host threads on one device) race on the table.
+
+static __device__ __align__(256) int32_t sv_kmap_static_table[2 * SV_KMAP_STATIC_MAX_ROWS];
+
+namespace {
+std::mutex g_static_table_mu;
+int32_t* g_static_table_addr[256] = {};
+
+// Device address of sv_kmap_static_table on the current device. In host code the array's name
+// only stands in for the symbol, so the address is looked up once per device (with that device
+// current) and reused.
+int static_table_address(int32_t** out) {
+  int dev = 0;
+  SV_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 256) SV_FAIL(SV_ERR_UNSUPPORTED, "device index above 255");
+  std::lock_guard<std::mutex> lock(g_static_table_mu);
+  if (g_static_table_addr[dev] == nullptr) {
+    void* p = nullptr;
+    SV_CUDA_TRY(cudaGetSymbolAddress(&p, sv_kmap_static_table));
+    g_static_table_addr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_static_table_addr[dev];
+  return SV_OK;
+}
+}  // namespace
+
+extern "C" int sv_kmap_build_static(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                                    const int32_t dilation[3], int32_t* nbr, int32_t* status,
+                                    sv_stream_t stream) {
+  if (n > SV_KMAP_STATIC_MAX_ROWS)
+    SV_FAIL(SV_ERR_UNSUPPORTED,
+            "sv_kmap_build_static: at most " + std::to_string(SV_KMAP_STATIC_MAX_ROWS) +
+                " coordinate rows (got " + std::to_string(n) +
+                "); use sv_kmap_build with a caller-provided workspace");
+  const int64_t slots = sv_kmap_table_slots(n);  // <= 2 * SV_KMAP_STATIC_MAX_ROWS
+  int32_t* table = nullptr;
+  if (n > 0) {
+    const int rc = static_table_address(&table);
+    if (rc != SV_OK) return rc;
+  }
+  // sv_kmap_build clears the `slots` words it uses to -1 before inserting, so nothing of an
+  // earlier call's table survives into this one.
+  return sv_kmap_build(coords, n, kernel, dilation, nbr, slots, table,
+                       (size_t)slots * sizeof(int32_t), status, stream);
 }
