@@ -45,6 +45,11 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument(
+        "--profiling",
+        action="store_true",
+        help="for runs under ncu: skip the CPU baseline and the CUPTI launch count",
+    )
     return p.parse_args()
 
 
@@ -377,7 +382,7 @@ def run_ours(args) -> None:
         mid = torch.cuda.Event(enable_timing=True)
         step()
 
-    launches = count_launches(mid_step)
+    launches = None if args.profiling else count_launches(mid_step)
 
     stats = torch.tensor([mean_step, mean_conv, mean_e2e, float(n), float(pairs)],
                          dtype=torch.float64, device=dev)
@@ -440,7 +445,7 @@ def run_ours(args) -> None:
             "gpu_launches": None if launches is None else launches * args.steps,
             "clocks": clocks,
         }
-        if world == 1:
+        if world == 1 and not args.profiling:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     if world > 1:
