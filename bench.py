@@ -21,9 +21,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -195,61 +193,73 @@ def run_reference(args) -> None:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples taken while the timed region runs."""
+    """SM clock and throttle reasons sampled (NVML, every 2 ms) while the timed region runs."""
 
-    FIELDS = (
-        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-        "clocks_event_reasons.sw_power_cap"
-    )
+    REASONS = {
+        0x8: "hw_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x20: "sw_thermal_slowdown",
+        0x4: "sw_power_cap",
+        0x80: "hw_power_brake_slowdown",
+    }
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.proc = None
+    def __init__(self, cuda_index: int):
+        import threading
+
+        self.samples: list[tuple[float, int]] = []
+        self.stop_evt = threading.Event()
+        self.thread = None
+        self.handle = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+        except Exception:
+            self.handle = None
+
+    def _run(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
+            nv, "nvmlDeviceGetCurrentClocksThrottleReasons"
+        )
+        while not self.stop_evt.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                self.samples.append((mhz, int(get_reasons(self.handle))))
+            except Exception:
+                pass
+            self.stop_evt.wait(0.002)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.gpu)],
-                stdout=self.file, stderr=subprocess.DEVNULL,
-            )
-        except OSError:
-            self.proc = None
+        import threading
+
+        if self.handle is not None:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
 
     def stop(self) -> dict | None:
-        if self.proc is None:
+        if self.thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.file.flush()
-        self.file.seek(0)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for row in self.file.read().strip().splitlines():
-            cols = [c.strip() for c in row.split(",")]
-            if len(cols) < 8:
-                continue
-            try:
-                sm.append(float(cols[1]))
-                mx.append(float(cols[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, cols[4:8]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        os.unlink(self.file.name)
-        if not sm:
+        self.stop_evt.set()
+        self.thread.join(timeout=5)
+        if not self.samples:
             return None
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
         return {
-            "sm_mhz": statistics.median(sm),
-            "sm_max_mhz": max(mx),
-            "reasons": sorted(reasons),
-            "samples": len(sm),
+            "sm_mhz": statistics.median(m for m, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(name for bit, name in self.REASONS.items() if bits & bit),
+            "samples": len(self.samples),
+            "source": "nvml, 2 ms",
         }
 
 
