@@ -15,11 +15,12 @@
 //               matrix, K-major, 128-byte swizzle, one tiled 2-D load per stage;
 //   warp 1      TMEM allocator and the single thread that issues tcgen05.mma (M=128,
 //               N=BN, K=16, four per stage) and tcgen05.commit;
-//   warps 2-5   gatherers: thread r copies the 128-byte slice of its row's neighbour
-//               features into the A stage with cp.async (16 B each, zero-filled when the
-//               neighbour is missing), writing the same 128-byte swizzle TMA would; then the
-//               epilogue: tcgen05.ld of 32 accumulator columns at a time, + bias, round,
-//               and 16-byte stores to the row's output.
+//   warps 2-5   gatherers: the A stage (128 neighbour rows x 128 bytes) is copied with
+//               16-byte cp.async, eight threads per row so each warp instruction reads four
+//               whole rows (zero-filled when the neighbour is missing), into the same 128-byte
+//               swizzle TMA would write. Then the same warps run the epilogue: tcgen05.ld of
+//               32 accumulator columns at a time, + bias, round, 16-byte stores to the row's
+//               output.
 // Stages are a 4-deep ring of (A 16 KB, B BN*128 B) guarded by full/empty mbarriers. Every
 // wait is bounded: on expiry the kernel ORs SV_DEVICE_WAIT_TIMEOUT into the status word,
 // drains its own copies and frees TMEM.
@@ -120,14 +121,19 @@ __global__ void __launch_bounds__(TTHREADS, 1)
       }
     }
     s_orow[r] = orow;
-    for (int k = 0; k < kvol; ++k) {
-      int32_t v = orow >= 0 ? __ldg(&nbr[(int64_t)orow * kvol + k]) : -1;
-      if (v >= n) {
-        report(status, SV_DEVICE_BAD_INDEX);
-        v = -1;
+    // independent loads (unrolled to the 27-offset bound) so their latencies overlap
+    const int32_t* nrow = nbr + (int64_t)(orow >= 0 ? orow : 0) * kvol;
+#pragma unroll
+    for (int k = 0; k < TMAX_KVOL; ++k) {
+      if (k < kvol) {
+        int32_t v = orow >= 0 ? __ldg(&nrow[k]) : -1;
+        if (v >= n) {
+          report(status, SV_DEVICE_BAD_INDEX);
+          v = -1;
+        }
+        s_nbr[r * TMAX_KVOL + k] = v;
+        my_mask |= (uint32_t)(v >= 0) << k;
       }
-      s_nbr[r * TMAX_KVOL + k] = v;
-      my_mask |= (uint32_t)(v >= 0) << k;
     }
   }
   __syncthreads();
@@ -190,15 +196,23 @@ __global__ void __launch_bounds__(TTHREADS, 1)
     }
   } else {
     // ---- gather ----
-    const int r = threadIdx.x - 64;
-    const uint32_t rx = r & 7;
-    const int32_t* my_nbr = s_nbr + r * TMAX_KVOL;
+    // Gatherer g copies 16-byte chunk (g % 8) of tile rows g/8 + 16*i, i = 0..7: one warp
+    // instruction moves four whole 128-byte rows, so every L2 sector it touches is used in full.
+    const int g = threadIdx.x - 64;
+    const uint32_t chunk = g & 7;
+    const int row0 = g >> 3;
+    const uint32_t swz = ((chunk ^ (uint32_t)(row0 & 7)) << 4);  // (row0 + 16*i) & 7 == row0 & 7
     int it = 0;
     for (uint32_t m = umask; m != 0 && ok; m &= m - 1) {
       const int k = __ffs(m) - 1;
-      const int32_t src = my_nbr[k];
-      const T* row = feat + (src >= 0 ? (int64_t)src * cin : 0);
-      const uint32_t nbytes = src >= 0 ? 16u : 0u;
+      const T* src[8];
+      uint32_t nbytes[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int32_t s_row = s_nbr[(row0 + 16 * i) * TMAX_KVOL + k];
+        src[i] = feat + (s_row >= 0 ? (int64_t)s_row * cin : 0) + chunk * 8;
+        nbytes[i] = s_row >= 0 ? 16u : 0u;
+      }
       for (int kb = 0; kb < kb_per_k; ++kb, ++it) {
         const int slot = it % TSTAGES;
         const uint32_t ph = (it / TSTAGES) & 1;
@@ -206,11 +220,10 @@ __global__ void __launch_bounds__(TTHREADS, 1)
           ok = false;
           break;
         }
-        const uint32_t dst = smem_u32(sA + slot * A_STAGE_BYTES) + (uint32_t)r * 128u;
-        const T* gp = row + kb * TBK;
+        const uint32_t dst = smem_u32(sA + slot * A_STAGE_BYTES) + (uint32_t)row0 * 128u + swz;
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          cp_async_16(dst + (((uint32_t)c ^ rx) << 4), gp + c * 8, nbytes);
+        for (int i = 0; i < 8; ++i)
+          cp_async_16(dst + (uint32_t)(16 * i) * 128u, src[i] + kb * TBK, nbytes[i]);
         cp_async_arrive_noinc(&full[slot]);
       }
     }
