@@ -321,7 +321,7 @@ def run_ours(args) -> None:
         x = SparseTensor(feats, coords, SHELLS_PER_GPU, spatial)
         nbr = build_neighbor_map(x.coords, 3)
         x.cache[key] = nbr
-        x.cache[plan_key] = conv_row_order(nbr)
+        x.cache[plan_key] = conv_row_order(nbr)  # (row_order, tile_order)
         mid.record()
         return conv(x)
 

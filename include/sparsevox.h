@@ -104,26 +104,33 @@ SV_API int sv_kmap_build_static(const int32_t* coords, int64_t n, const int32_t 
                                 const int32_t dilation[3], int32_t* nbr, int32_t* status,
                                 sv_stream_t stream);
 
-/* Row schedule for the tensor-core convolution: a permutation of 0..n-1 that groups rows with
- * equal neighbour-validity masks (stable, so rows with one mask keep their spatial order).
+/* Schedule for the tensor-core convolution, derived from a kernel map:
+ *  row_order [n]: a permutation of 0..n-1 that groups rows with equal neighbour-validity masks
+ *                 (stable, so rows with one mask keep their spatial order);
+ *  tile_order [sv_conv_plan_tiles(n)] (nullable): the 128-row tiles of row_order, the ones
+ *                 with the most neighbour offsets first (the convolution starts long work early).
  * Needs kvol <= 32. Workspace: sv_conv_plan_workspace_bytes(n). */
+SV_API int64_t sv_conv_plan_tiles(int64_t n);
 SV_API size_t sv_conv_plan_workspace_bytes(int64_t n);
 SV_API int sv_conv_plan(const int32_t* nbr, int64_t n, int kvol, int32_t* row_order,
-                        void* workspace, size_t workspace_bytes, sv_stream_t stream);
+                        int32_t* tile_order, void* workspace, size_t workspace_bytes,
+                        sv_stream_t stream);
 
 /* ---- convolution (sparse_conv3d / SparseConv3D.__call__) ------------------------------ */
 
 /* out[p, o] = bias[o] + sum_k sum_i features[nbr[p,k], i] * W[k, i, o] over nbr[p,k] >= 0,
  * accumulated in fp32 and rounded once to `dtype` (the Metal kernel's semantics,
  * src/mlx_diffuser/kernels/sparse.py:14-34). features [n, cin], weight in `layout`, bias
- * [cout] (nullable = zero), out [n, cout]; all of `dtype`. row_order (nullable) is a
- * permutation from sv_conv_plan that only changes the schedule, never the result.
- * A KIO weight on the tensor-core path is repacked into `workspace`
- * (sv_conv3d_workspace_bytes bytes); otherwise workspace may be null. */
+ * [cout] (nullable = zero), out [n, cout]; all of `dtype`. row_order and tile_order
+ * (nullable) come from sv_conv_plan and only change the schedule, never the result.
+ * The tensor-core path needs sv_conv3d_workspace_bytes() of workspace (a scheduler word, plus
+ * the repacked weight for a KIO layout); the CUDA-core path needs none (0 bytes, may be null).
+ * Calls that share one workspace must not overlap on the GPU. */
 SV_API size_t sv_conv3d_workspace_bytes(int64_t n, int cin, int cout, int kvol, int dtype,
                                         int layout, int algo);
 SV_API int sv_conv3d_forward(const void* features, int64_t n, int cin, const int32_t* nbr,
-                             int kvol, const int32_t* row_order, const void* weight, int layout,
+                             int kvol, const int32_t* row_order, const int32_t* tile_order,
+                             const void* weight, int layout,
                              const void* bias, int cout, int dtype, void* out, int algo,
                              void* workspace, size_t workspace_bytes, int32_t* status,
                              sv_stream_t stream);

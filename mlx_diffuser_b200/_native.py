@@ -51,12 +51,13 @@ _SIGNATURES = {
     "sv_kmap_workspace_bytes": (_SZ, [_I64]),
     "sv_kmap_build": (_I32, [_P, _I64, _P, _P, _P, _I64, _P, _SZ, _P, _P]),
     "sv_kmap_build_static": (_I32, [_P, _I64, _P, _P, _P, _P, _P]),
+    "sv_conv_plan_tiles": (_I64, [_I64]),
     "sv_conv_plan_workspace_bytes": (_SZ, [_I64]),
-    "sv_conv_plan": (_I32, [_P, _I64, _I32, _P, _P, _SZ, _P]),
+    "sv_conv_plan": (_I32, [_P, _I64, _I32, _P, _P, _P, _SZ, _P]),
     "sv_conv3d_workspace_bytes": (_SZ, [_I64, _I32, _I32, _I32, _I32, _I32, _I32]),
     "sv_conv3d_forward": (
         _I32,
-        [_P, _I64, _I32, _P, _I32, _P, _P, _I32, _P, _I32, _I32, _P, _I32, _P, _SZ, _P, _P],
+        [_P, _I64, _I32, _P, _I32, _P, _P, _P, _I32, _P, _I32, _I32, _P, _I32, _P, _SZ, _P, _P],
     ),
     "sv_weight_kio_to_oki": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P]),
     "sv_downsample_workspace_bytes": (_SZ, [_I64]),

@@ -65,7 +65,7 @@ extern "C" int sv_abi_version(void) { return 1; }
 
 extern "C" size_t sv_conv3d_workspace_bytes(int64_t n, int cin, int cout, int kvol, int dtype,
                                             int layout, int algo) {
-  if (layout != SV_WEIGHT_KIO || !valid_dtype(dtype)) return 0;
+  if (!valid_dtype(dtype) || (layout != SV_WEIGHT_KIO && layout != SV_WEIGHT_OKI)) return 0;
   ConvArgs a{};
   a.n = n;
   a.cin = cin;
@@ -75,7 +75,10 @@ extern "C" size_t sv_conv3d_workspace_bytes(int64_t n, int cin, int cout, int kv
   a.layout = layout;
   a.features = a.out = reinterpret_cast<void*>(uintptr_t(256));
   if (!tc_path(a, algo)) return 0;
-  return align_up((size_t)kvol * cin * cout * dtype_size(dtype), 256);
+  // scheduler word, then (for a KIO weight) the repacked weight
+  const size_t repack =
+      layout == SV_WEIGHT_KIO ? align_up((size_t)kvol * cin * cout * dtype_size(dtype), 256) : 0;
+  return 256 + repack;
 }
 
 extern "C" int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int cout, int dtype,
@@ -88,7 +91,8 @@ extern "C" int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int co
 }
 
 extern "C" int sv_conv3d_forward(const void* features, int64_t n, int cin, const int32_t* nbr,
-                                 int kvol, const int32_t* row_order, const void* weight,
+                                 int kvol, const int32_t* row_order, const int32_t* tile_order,
+                                 const void* weight,
                                  int layout, const void* bias, int cout, int dtype, void* out,
                                  int algo, void* workspace, size_t workspace_bytes,
                                  int32_t* status, sv_stream_t stream) {
@@ -111,16 +115,18 @@ extern "C" int sv_conv3d_forward(const void* features, int64_t n, int cin, const
             "tcgen05 convolution needs fp16/bf16, Cin % 64 == 0, Cout % 32 == 0, kernel volume "
             "<= 27 and 16-byte aligned features/weight/out");
   if (!use_tc) return conv_simt_launch(a, s);
+  const size_t need = sv_conv3d_workspace_bytes(n, cin, cout, kvol, dtype, layout, algo);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    SV_FAIL(SV_ERR_WORKSPACE,
+            "sv_conv3d_forward: the tcgen05 path needs sv_conv3d_workspace_bytes() of workspace");
+  int32_t* counter = static_cast<int32_t*>(workspace);
   if (layout == SV_WEIGHT_KIO) {
-    const size_t need = (size_t)kvol * cin * cout * dtype_size(dtype);
-    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
-      SV_FAIL(SV_ERR_WORKSPACE,
-              "sv_conv3d_forward: a (K, Cin, Cout) weight on the tcgen05 path needs "
-              "sv_conv3d_workspace_bytes() of workspace");
-    int rc = transpose(weight, (int64_t)kvol * cin, cout, dtype_size(dtype), workspace, s);
+    void* packed = static_cast<uint8_t*>(workspace) + 256;
+    int rc = transpose(weight, (int64_t)kvol * cin, cout, dtype_size(dtype), packed, s);
     if (rc != SV_OK) return rc;
-    a.weight = workspace;
+    a.weight = packed;
     a.layout = SV_WEIGHT_OKI;
   }
-  return conv_tc_launch(a, s);
+  // tile_order only makes sense together with the row schedule it was derived from
+  return conv_tc_launch(a, row_order ? tile_order : nullptr, counter, s);
 }

@@ -25,7 +25,10 @@ struct ConvArgs {
 int conv_simt_launch(const ConvArgs& a, cudaStream_t s);
 
 // tcgen05 kernel: fp16/bf16, OKI weight layout, shapes accepted by conv_tc_supported().
+// `tile_order` (nullable) lists the 128-row tiles of `row_order`, most expensive first;
+// `counter` is one device word the persistent scheduler hands out work items from.
 bool conv_tc_supported(const ConvArgs& a);
-int conv_tc_launch(const ConvArgs& a, cudaStream_t s);
+int conv_tc_launch(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
+                   cudaStream_t s);
 
 }  // namespace sv

@@ -9,6 +9,7 @@
 //    atomicMax on the slot: the largest row index among equal rows wins;
 //  * offsets are enumerated in the reference's order (:160-169); a neighbour coordinate that
 //    leaves the int32 range simply misses, as a Python dict lookup of that tuple would.
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -108,6 +109,24 @@ __global__ void row_mask_kernel(const int32_t* __restrict__ nbr, int64_t n, int 
   rows[p] = (int32_t)p;
 }
 
+// Cost of each 128-row tile of the schedule: the number of offsets the tensor-core kernel
+// visits for it (popcount of the union of its rows' masks), stored as 32 - cost so that an
+// ascending sort lists the most expensive tiles first.
+__global__ void tile_cost_kernel(const uint32_t* __restrict__ masks_sorted, int64_t n,
+                                 int64_t tiles, uint32_t* __restrict__ keys,
+                                 int32_t* __restrict__ ids) {
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= tiles) return;
+  uint32_t u = 0;
+  for (int64_t r = t * 128 + lane; r < min(n, (t + 1) * 128); r += 32) u |= masks_sorted[r];
+  u = __reduce_or_sync(0xffffffffu, u);
+  if (lane == 0) {
+    keys[t] = 32u - (uint32_t)__popc(u);
+    ids[t] = (int32_t)t;
+  }
+}
+
 size_t plan_cub_bytes(int64_t n) {
   size_t bytes = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
@@ -165,13 +184,28 @@ extern "C" int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t ker
   return SV_OK;
 }
 
+extern "C" int64_t sv_conv_plan_tiles(int64_t n) { return n > 0 ? (n + 127) / 128 : 0; }
+
+namespace {
+size_t plan_tile_cub_bytes(int64_t tiles) {
+  size_t bytes = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                  (const int32_t*)nullptr, (int32_t*)nullptr, (int)tiles, 0, 6);
+  return bytes;
+}
+}  // namespace
+
 extern "C" size_t sv_conv_plan_workspace_bytes(int64_t n) {
   if (n <= 0) return 0;
-  return align_up((size_t)n * 4, 256) * 3 + align_up(plan_cub_bytes(n), 256);
+  const int64_t tiles = sv_conv_plan_tiles(n);
+  // row masks, sorted masks, row ids; tile keys, sorted tile keys, tile ids; CUB scratch
+  return align_up((size_t)n * 4, 256) * 3 + align_up((size_t)tiles * 4, 256) * 3 +
+         align_up(std::max(plan_cub_bytes(n), plan_tile_cub_bytes(tiles)), 256);
 }
 
 extern "C" int sv_conv_plan(const int32_t* nbr, int64_t n, int kvol, int32_t* row_order,
-                            void* workspace, size_t workspace_bytes, sv_stream_t stream) {
+                            int32_t* tile_order, void* workspace, size_t workspace_bytes,
+                            sv_stream_t stream) {
   if (n < 0 || kvol <= 0) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv_plan: bad sizes");
   if (kvol > 32) SV_FAIL(SV_ERR_UNSUPPORTED, "sv_conv_plan: kernel volume above 32");
   if (n == 0) return SV_OK;
@@ -181,17 +215,30 @@ extern "C" int sv_conv_plan(const int32_t* nbr, int64_t n, int kvol, int32_t* ro
   if (workspace == nullptr || workspace_bytes < sv_conv_plan_workspace_bytes(n))
     SV_FAIL(SV_ERR_WORKSPACE, "sv_conv_plan: workspace too small");
   cudaStream_t s = to_stream(stream);
+  const int64_t tiles = sv_conv_plan_tiles(n);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const size_t vec = align_up((size_t)n * 4, 256);
+  const size_t tvec = align_up((size_t)tiles * 4, 256);
   uint32_t* masks = reinterpret_cast<uint32_t*>(ws);
   uint32_t* masks_sorted = reinterpret_cast<uint32_t*>(ws + vec);
   int32_t* rows = reinterpret_cast<int32_t*>(ws + 2 * vec);
-  void* cub_tmp = ws + 3 * vec;
-  size_t cub_bytes = workspace_bytes - 3 * vec;
+  uint32_t* tkeys = reinterpret_cast<uint32_t*>(ws + 3 * vec);
+  uint32_t* tkeys_sorted = reinterpret_cast<uint32_t*>(ws + 3 * vec + tvec);
+  int32_t* tids = reinterpret_cast<int32_t*>(ws + 3 * vec + 2 * tvec);
+  void* cub_tmp = ws + 3 * vec + 3 * tvec;
+  size_t cub_bytes = workspace_bytes - (3 * vec + 3 * tvec);
   row_mask_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(nbr, n, kvol, masks, rows);
   SV_LAUNCH_CHECK();
   SV_CUDA_TRY(cub::DeviceRadixSort::SortPairs(cub_tmp, cub_bytes, masks, masks_sorted, rows,
                                               row_order, (int)n, 0, kvol, s));
+  if (tile_order != nullptr) {
+    tile_cost_kernel<<<(unsigned)((tiles + 7) / 8), 256, 0, s>>>(masks_sorted, n, tiles, tkeys,
+                                                                 tids);
+    SV_LAUNCH_CHECK();
+    size_t tile_cub_bytes = cub_bytes;
+    SV_CUDA_TRY(cub::DeviceRadixSort::SortPairs(cub_tmp, tile_cub_bytes, tkeys, tkeys_sorted,
+                                                tids, tile_order, (int)tiles, 0, 6, s));
+  }
   return SV_OK;
 }
 

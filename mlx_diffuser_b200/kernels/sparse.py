@@ -39,11 +39,13 @@ def conv3d_forward(
     cout: int,
     *,
     row_order: torch.Tensor | None = None,
+    tile_order: torch.Tensor | None = None,
     algo: int = N.SV_CONV_AUTO,
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Call ``sv_conv3d_forward``. Tensors must already be contiguous, on one CUDA device, and
-    share the feature dtype (``neighbors`` int32); ``layout`` is SV_WEIGHT_KIO or _OKI."""
+    share the feature dtype (``neighbors`` int32); ``layout`` is SV_WEIGHT_KIO or _OKI.
+    ``row_order`` / ``tile_order`` are the schedule from :func:`conv_row_order`."""
 
     n, cin = features.shape
     kvol = neighbors.shape[1]
@@ -63,6 +65,7 @@ def conv3d_forward(
         neighbors.data_ptr(),
         kvol,
         N.ptr(row_order),
+        N.ptr(tile_order),
         weight.data_ptr(),
         layout,
         N.ptr(bias),

@@ -217,22 +217,24 @@ def build_neighbor_map(
     return out
 
 
-def conv_row_order(neighbors: torch.Tensor) -> torch.Tensor | None:
-    """Row schedule for the tensor-core convolution (rows grouped by neighbour mask), or None
-    when the kernel volume exceeds 32."""
+def conv_row_order(neighbors: torch.Tensor) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+    """Schedule for the tensor-core convolution: ``(row_order, tile_order)``. Rows are grouped
+    by neighbour mask; the 128-row tiles are listed most expensive first. ``(None, None)`` when
+    the kernel volume exceeds 32 (the convolution then runs in plain row order)."""
 
     n, kvol = neighbors.shape
     if n == 0 or kvol > 32:
-        return None
+        return None, None
     lib = N.load()
     dev = neighbors.device
     order = torch.empty(n, dtype=torch.int32, device=dev)
+    tiles = torch.empty(int(lib.sv_conv_plan_tiles(n)), dtype=torch.int32, device=dev)
     ws_bytes = lib.sv_conv_plan_workspace_bytes(n)
     ws = N.workspace(ws_bytes, dev)
-    rc = lib.sv_conv_plan(neighbors.data_ptr(), n, kvol, order.data_ptr(), ws.data_ptr(),
-                          ws_bytes, N.stream(dev))
+    rc = lib.sv_conv_plan(neighbors.data_ptr(), n, kvol, order.data_ptr(), tiles.data_ptr(),
+                          ws.data_ptr(), ws_bytes, N.stream(dev))
     N.check(rc, "conv row schedule")
-    return order
+    return order, tiles
 
 
 class _SparseConv3DCore(nn.Module):
@@ -320,9 +322,10 @@ class SparseConv3D(nn.Module):
                 f"({neighbors.shape[1]}, {features.shape[1]}, Cout), got "
                 f"({self.kernel_size**3}, {i}, {o})"
             )
+        row_order, tile_order = x.cache[plan_key]
         out = conv3d_forward(
             features.contiguous(), neighbors, weight, N.SV_WEIGHT_OKI, bias, o,
-            row_order=x.cache[plan_key], algo=self.algo,
+            row_order=row_order, tile_order=tile_order, algo=self.algo,
         )
         return x.replace(out)
 

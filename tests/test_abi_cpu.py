@@ -52,7 +52,9 @@ def test_abi_version_and_sizes():
     # KIO weight on a tensor-core shape needs a repack workspace; OKI needs none
     kio = lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 2, N.SV_WEIGHT_KIO, N.SV_CONV_AUTO)
     assert kio >= 27 * 64 * 64 * 2
-    assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 2, N.SV_WEIGHT_OKI, N.SV_CONV_AUTO) == 0
+    # the tensor-core path always needs its scheduler word; the CUDA-core path nothing
+    assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 2, N.SV_WEIGHT_OKI, N.SV_CONV_AUTO) == 256
+    assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 2, N.SV_WEIGHT_OKI, N.SV_CONV_SIMT) == 0
     assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 0, N.SV_WEIGHT_KIO, N.SV_CONV_AUTO) == 0
     assert lib.sv_conv3d_workspace_bytes(100, 8, 64, 27, 2, N.SV_WEIGHT_KIO, N.SV_CONV_AUTO) == 0
 
@@ -64,14 +66,14 @@ def test_argument_errors_are_reported_before_any_launch():
     rc = lib.sv_kmap_build(None, 10, k, d, None, 64, None, 0, None, None)
     assert rc == N.SV_ERR_BAD_SHAPE
     assert "odd" in lib.sv_last_error().decode()
-    rc = lib.sv_conv3d_forward(None, 5, 8, None, 27, None, None, 0, None, 8, 7, None, 0, None, 0,
+    rc = lib.sv_conv3d_forward(None, 5, 8, None, 27, None, None, None, 0, None, 8, 7, None, 0, None, 0,
                                None, None)
     assert rc == N.SV_ERR_BAD_DTYPE
-    rc = lib.sv_conv3d_forward(None, 5, 8, None, 27, None, None, 0, None, 8, 2, None, 9, None, 0,
+    rc = lib.sv_conv3d_forward(None, 5, 8, None, 27, None, None, None, 0, None, 8, 2, None, 9, None, 0,
                                None, None)
     assert rc == N.SV_ERR_INVALID_ARGUMENT
     # nothing to do -> OK without touching the device
-    assert lib.sv_conv3d_forward(None, 0, 8, None, 27, None, None, 0, None, 8, 2, None, 0, None, 0,
+    assert lib.sv_conv3d_forward(None, 0, 8, None, 27, None, None, None, 0, None, 8, 2, None, 0, None, 0,
                                  None, None) == N.SV_OK
     m = ctypes.c_int64(-1)
     assert lib.sv_downsample_coords(None, 0, 2, None, None, None, None, ctypes.byref(m), None, 0,

@@ -112,6 +112,21 @@ def test_tcgen05_shapes(cin, cout, dtype):
     assert max_rel_err(out, ref) <= HALF_TOL
 
 
+@pytest.mark.parametrize("cout", [64, 128, 256])
+def test_tcgen05_persistent_ctas_take_several_items(cout):
+    """24k rows give more work items than SMs, so each persistent CTA runs several items and
+    reuses both accumulator buffers and both work slots; every item must match the reference."""
+
+    coords = scenes.shell32_batch(4)
+    dtype = torch.bfloat16
+    f = _rounded(scenes.normal_features(len(coords), 64, seed=31), dtype)
+    w = _rounded(scenes.conv_weight(cout, 64, 3, seed=32), dtype)
+    b = _rounded(np.random.default_rng(33).standard_normal(cout).astype(np.float32), dtype)
+    ref = O.sparse_conv3d(f, O.build_neighbor_map(coords, 3), O.spconv_weight_to_kio(w), b)
+    out, _ = _run(coords, f, w, b, dtype, algo=N.SV_CONV_TCGEN05)
+    assert max_rel_err(out, ref) <= HALF_TOL
+
+
 def test_tcgen05_agrees_with_simt_and_ignores_row_order():
     coords = scenes.shell32_batch(2)
     cin = cout = 128
@@ -120,10 +135,10 @@ def test_tcgen05_agrees_with_simt_and_ignores_row_order():
     w = torch.from_numpy(scenes.conv_weight(cout, cin, 3, seed=6)).to(DEV, dtype).contiguous()
     b = torch.zeros(cout, device=DEV, dtype=dtype)
     nbr = build_neighbor_map(torch.from_numpy(coords).to(DEV), 3)
-    order = conv_row_order(nbr)
+    order, tiles = conv_row_order(nbr)
     tc_plain = conv3d_forward(feats, nbr, w, N.SV_WEIGHT_OKI, b, cout, algo=N.SV_CONV_TCGEN05)
     tc_order = conv3d_forward(feats, nbr, w, N.SV_WEIGHT_OKI, b, cout, row_order=order,
-                              algo=N.SV_CONV_TCGEN05)
+                              tile_order=tiles, algo=N.SV_CONV_TCGEN05)
     simt = conv3d_forward(feats, nbr, w, N.SV_WEIGHT_OKI, b, cout, row_order=order,
                           algo=N.SV_CONV_SIMT)
     N.check_device_status(DEV)

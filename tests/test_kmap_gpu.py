@@ -98,7 +98,8 @@ def test_kmap_undersized_table_raises():
 def test_conv_row_order_groups_rows_by_mask():
     coords = scenes.shell32_batch(2)
     nbr = build_neighbor_map(torch.from_numpy(coords).to(DEV), 3)
-    order = conv_row_order(nbr).cpu().numpy()
+    order_t, tiles_t = conv_row_order(nbr)
+    order = order_t.cpu().numpy()
     n = len(coords)
     assert np.array_equal(np.sort(order), np.arange(n))
     host = nbr.cpu().numpy()
@@ -107,5 +108,10 @@ def test_conv_row_order_groups_rows_by_mask():
     assert (np.diff(m) >= 0).all()
     same = np.diff(m) == 0
     assert (np.diff(order)[same] > 0).all()  # stable: spatial order kept inside a group
-    assert conv_row_order(build_neighbor_map(torch.from_numpy(coords).to(DEV), 5)) is None
+    # tiles listed most expensive first: non-increasing union popcount, a permutation
+    tiles = tiles_t.cpu().numpy()
+    assert np.array_equal(np.sort(tiles), np.arange(-(-n // 128)))
+    cost = [bin(int(np.bitwise_or.reduce(m[t * 128:(t + 1) * 128]))).count("1") for t in tiles]
+    assert all(a >= b for a, b in zip(cost, cost[1:]))
+    assert conv_row_order(build_neighbor_map(torch.from_numpy(coords).to(DEV), 5)) == (None, None)
     N.check_device_status(DEV)
