@@ -44,6 +44,16 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument(
+        "--workload",
+        choices=["conv1024", "kmap", "pool", "scene128", "sweep"],
+        default="conv1024",
+        help="conv1024 (default): the headline line above. The others run on one GPU and "
+        "print one line each: kmap = kernel-map build on 16 x 128^3 at 8%% occupancy; pool = "
+        "downsample + upsample of the 237k-voxel 128^3 scene at 128 channels; scene128 = "
+        "convs 64->64->32 on that scene; sweep = map build and conv over occupancy "
+        "{0.5, 2, 8, 30}%% x grid {64, 128}^3 x width {32, 128, 512, 1024}, batch 16",
+    )
+    p.add_argument(
         "--profiling",
         action="store_true",
         help="for runs under ncu: skip the CPU baseline and the CUPTI launch count",
@@ -463,10 +473,168 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------------------------
+# secondary workloads (one GPU)
+# ---------------------------------------------------------------------------------------------
+
+
+def _time_device(fn, steps: int, warmup: int, flush) -> float:
+    """Mean milliseconds of fn() over `steps` runs, CUDA events, L2 flushed before each run."""
+
+    import torch
+
+    for _ in range(max(warmup, 1)):
+        fn()
+    total = 0.0
+    for _ in range(steps):
+        flush.fill_(1.0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        total += a.elapsed_time(b)
+    return total / steps
+
+
+def _line(metric, value, unit, ms, args, config, roofline=None) -> dict:
+    return {
+        "metric": metric,
+        "value": value,
+        "unit": unit,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "data": "synthetic",
+        "config": config,
+        "roofline": roofline,
+    }
+
+
+def _hbm_roofline(bytes_per_launch: float, ms: float, kernel: str) -> dict:
+    peaks = measured_peaks()
+    achieved = bytes_per_launch / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peaks["hbm_gbs"],
+            "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+            "peak_source": peaks["source"], "algorithmic_bytes": bytes_per_launch}
+
+
+def run_workload(args) -> None:
+    import torch
+
+    from mlx_diffuser_b200 import _native as N
+    from mlx_diffuser_b200 import scenes
+    from mlx_diffuser_b200.layers.sparse import (
+        SparseConv3D,
+        SparseTensor,
+        build_neighbor_map,
+        sparse_downsample,
+        sparse_upsample,
+    )
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def conv_case(coords, cin, cout, dtype, seed):
+        n = len(coords)
+        c = torch.from_numpy(coords).to(dev)
+        f = torch.from_numpy(scenes.normal_features(n, cin, seed)).to(dev, dtype)
+        conv = SparseConv3D(cin, cout, 3).to(dev)
+        conv.conv.weight = torch.from_numpy(scenes.conv_weight(cout, cin, 3, seed + 1)).to(dev, dtype)
+        conv.conv.bias = torch.zeros(cout, device=dev, dtype=dtype)
+        x = SparseTensor(f, c, int(coords[:, 0].max()) + 1, None)
+        conv(x)  # builds and caches the map and schedule
+        nbr = x.cache["neighbors_3_1_(1, 1, 1)"]
+        pairs = int((nbr >= 0).sum().item())
+        ms = _time_device(lambda: conv(x), args.steps, args.warmup, flush)
+        flops = 2.0 * cin * cout * pairs
+        dsz = torch.finfo(dtype).bits // 8
+        bytes_ = dsz * n * (cin + cout) + dsz * 27 * cin * cout + 4 * 27 * n
+        peaks = measured_peaks()
+        t_tensor = flops / (peaks["bf16_tflops"] * 1e12)
+        t_hbm = bytes_ / (peaks["hbm_gbs"] * 1e9)
+        bound = "tensor" if t_tensor >= t_hbm else "hbm"
+        roof = (
+            {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
+             "unit": "TFLOP/s"}
+            if bound == "tensor"
+            else {"bound": "hbm", "achieved": bytes_ / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                  "unit": "GB/s"}
+        )
+        roof["frac"] = roof["achieved"] / roof["peak"]
+        roof["roofline_ms"] = max(t_tensor, t_hbm) * 1e3
+        roof["frac_of_roofline_time"] = roof["roofline_ms"] / ms
+        return ms, pairs, x, roof
+
+    def map_case(coords):
+        c = torch.from_numpy(coords).to(dev)
+        n = len(coords)
+        ms = _time_device(lambda: build_neighbor_map(c, 3), args.steps, args.warmup, flush)
+        return ms, _hbm_roofline(16.0 * n + 4.0 * 27 * n, ms, "kmap_insert + kmap_probe")
+
+    lines = []
+    if args.workload == "kmap":
+        coords = scenes.batched([scenes.uniform(128, 0.08, 500 + b) for b in range(16)])
+        ms, roof = map_case(coords)
+        lines.append(_line("kernel-map build voxels/s", len(coords) / (ms * 1e-3), "voxels/s", ms,
+                           args, {"workload": "kmap_uniform128x16_8pct", "voxels": len(coords)},
+                           roof))
+    elif args.workload == "pool":
+        coords = scenes.scene128(0)
+        n, ch = len(coords), 128
+        x = SparseTensor(torch.from_numpy(scenes.normal_features(n, ch, 3)).to(dev, torch.bfloat16),
+                         torch.from_numpy(coords).to(dev))
+        down = sparse_downsample(x, 2)
+        m = down.num_points
+        ms_down = _time_device(lambda: sparse_downsample(x, 2), args.steps, args.warmup, flush)
+        ms_up = _time_device(lambda: sparse_upsample(down, 2), args.steps, args.warmup, flush)
+        down_bytes = 16.0 * n + 16.0 * m + 4.0 * n + 2.0 * ch * (n + m)
+        up_bytes = 4.0 * n + 2.0 * ch * (m + n)
+        lines.append(_line("sparse_downsample voxels/s", n / (ms_down * 1e-3), "voxels/s", ms_down,
+                           args, {"workload": "scene128_pool_c128_bf16", "voxels": n, "coarse": m},
+                           _hbm_roofline(down_bytes, ms_down, "pool (coords sort + segment mean)")))
+        lines.append(_line("sparse_upsample voxels/s", n / (ms_up * 1e-3), "voxels/s", ms_up,
+                           args, {"workload": "scene128_pool_c128_bf16", "voxels": n, "coarse": m},
+                           _hbm_roofline(up_bytes, ms_up, "gather_rows_kernel")))
+    elif args.workload == "scene128":
+        coords = scenes.scene128(0)
+        for cin, cout in ((64, 64), (64, 32)):
+            ms, pairs, _, roof = conv_case(coords, cin, cout, torch.bfloat16, 11)
+            lines.append(_line("sparse conv3d active-voxels/s", len(coords) / (ms * 1e-3),
+                               "voxels/s", ms, args,
+                               {"workload": f"scene128_conv{cin}to{cout}_bf16",
+                                "voxels": len(coords), "valid_pairs": pairs}, roof))
+    elif args.workload == "sweep":
+        for grid in (64, 128):
+            for occ in (0.005, 0.02, 0.08, 0.30):
+                coords = scenes.batched([scenes.uniform(grid, occ, 700 + b) for b in range(16)])
+                ms_map, roof_map = map_case(coords)
+                for ch in (32, 128, 512, 1024):
+                    if len(coords) * ch > 4_000_000_000:
+                        continue  # keep features and output under 8 GB each
+                    ms, pairs, _, roof = conv_case(coords, ch, ch, torch.bfloat16, 13)
+                    lines.append(_line(
+                        "sparse conv3d active-voxels/s", len(coords) / (ms * 1e-3), "voxels/s",
+                        ms, args,
+                        {"workload": f"uniform{grid}x16_{occ:g}_c{ch}_bf16",
+                         "voxels": len(coords), "valid_pairs": pairs, "kmap_ms": ms_map,
+                         "kmap_roofline": roof_map}, roof))
+    for line in lines:
+        print(json.dumps(line), flush=True)
+    N.check_device_status(dev)
+
+
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "conv1024":
+        run_workload(args)
     else:
         run_ours(args)
 
