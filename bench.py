@@ -96,6 +96,18 @@ def profiled_traffic() -> float | None:
 # ---------------------------------------------------------------------------------------------
 
 
+def use_all_host_cores() -> None:
+    """The CPU baseline runs on every host core: torchrun exports OMP_NUM_THREADS=1 to its
+    ranks, so lift the BLAS thread limit explicitly."""
+
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+    except Exception:
+        pass
+
+
 def blas_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -126,6 +138,7 @@ def cpu_step(coords, feats, weight_kio, bias) -> None:
 def cpu_baseline(reps: int = 2) -> dict:
     from oracle import sparse_oracle as O
 
+    use_all_host_cores()
     coords, feats, weight = cpu_sample(0)
     wk = O.spconv_weight_to_kio(weight)
     bias = np.zeros(COUT, np.float32)
@@ -154,6 +167,7 @@ def run_reference(args) -> None:
         return
     from oracle import sparse_oracle as O
 
+    use_all_host_cores()
     coords, feats, weight = cpu_sample(0)
     wk = O.spconv_weight_to_kio(weight)
     bias = np.zeros(COUT, np.float32)

@@ -93,6 +93,7 @@ class HaloPlan:
     send_idx: list[torch.Tensor]
     recv_count: list[int]
     recv_offset: list[int]
+    schedule: tuple | None = None  # conv row schedule of local_nbr, built on first use
 
     @property
     def num_own(self) -> int:
@@ -179,3 +180,61 @@ class HaloPlan:
         if ops:
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
+
+
+# ---- GPU helpers ------------------------------------------------------------------------------
+
+
+def gather_rows(src: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """``src[index]`` for a CUDA ``[rows, C]`` tensor, through the library's row-gather kernel
+    (used to build the contiguous send buffers of :meth:`HaloPlan.exchange`)."""
+
+    from . import _native as N
+
+    src = src.contiguous()
+    idx = index.to(device=src.device, dtype=torch.int32).contiguous()
+    out = torch.empty((idx.numel(), src.shape[1]), dtype=src.dtype, device=src.device)
+    if idx.numel() == 0 or src.shape[1] == 0:
+        return out
+    code = N.DTYPE_CODE.get(src.dtype)
+    if code is None:
+        raise ValueError(f"gather_rows: unsupported dtype {src.dtype}")
+    rc = N.load().sv_upsample_features(
+        src.data_ptr(), src.shape[0], src.shape[1], code, idx.data_ptr(), idx.numel(),
+        out.data_ptr(), N.status_word(src.device).data_ptr(), N.stream(src.device),
+    )
+    N.check(rc, "gather_rows")
+    return out
+
+
+def halo_conv(
+    plan: HaloPlan,
+    local: torch.Tensor,
+    weight_oki: torch.Tensor,
+    bias: torch.Tensor | None,
+    *,
+    group=None,
+) -> torch.Tensor:
+    """One submanifold conv of a Morton-partitioned scene on this rank.
+
+    ``local`` is the rank's ``[own; halo]`` feature buffer (only the own rows need to be
+    filled); the halo rows are exchanged with NCCL point-to-point first, then the conv runs on
+    the local buffer with the plan's local map. Returns the outputs of the rank's own rows.
+    ``weight_oki`` is the spconv ``(O, k, k, k, I)`` weight in the feature dtype.
+    """
+
+    from .kernels.sparse import conv3d_forward
+    from . import _native as N
+    from .layers.sparse import conv_row_order
+
+    plan.exchange(local, gather=gather_rows, group=group)
+    if plan.local_nbr.device != local.device:
+        plan.local_nbr = plan.local_nbr.to(local.device)
+    nbr = plan.local_nbr
+    if plan.schedule is None:
+        plan.schedule = conv_row_order(nbr)
+    row_order, tile_order = plan.schedule
+    cout = weight_oki.shape[0]
+    out = conv3d_forward(local.contiguous(), nbr, weight_oki.contiguous(), N.SV_WEIGHT_OKI, bias,
+                         cout, row_order=row_order, tile_order=tile_order)
+    return out[: plan.num_own]
