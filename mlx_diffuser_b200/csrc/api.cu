@@ -112,7 +112,7 @@ extern "C" int sv_conv3d_forward(const void* features, int64_t n, int cin, const
   const bool use_tc = tc_path(a, algo) && aligned16(weight);
   if (algo == SV_CONV_TCGEN05 && !use_tc)
     SV_FAIL(SV_ERR_UNSUPPORTED,
-            "tcgen05 convolution needs fp16/bf16, Cin % 64 == 0, Cout % 32 == 0, kernel volume "
+            "tcgen05 convolution needs fp16/bf16, Cin % 32 == 0, Cout % 32 == 0, kernel volume "
             "<= 27 and 16-byte aligned features/weight/out");
   if (!use_tc) return conv_simt_launch(a, s);
   const size_t need = sv_conv3d_workspace_bytes(n, cin, cout, kvol, dtype, layout, algo);

@@ -244,16 +244,22 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
-// Shared-memory matrix descriptor for a K-major operand stored with the 128-byte swizzle:
-// rows of 128 bytes, 8-row (1024-byte) swizzle atoms stacked at a 1024-byte stride.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+// Shared-memory matrix descriptor for a K-major operand stored with a TMA-style swizzle:
+// rows of `row_bytes` (128 with the 128-byte swizzle, layout 2; 64 with the 64-byte swizzle,
+// layout 4), in 8-row swizzle atoms stacked at an 8 * row_bytes stride.
+__device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, uint32_t layout,
+                                                     uint32_t row_bytes) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);          // start address, bits [0,14)
-  d |= (uint64_t)(16u >> 4) << 16;                   // leading byte offset (unused for SW128 K-major)
-  d |= (uint64_t)(1024u >> 4) << 32;                 // stride byte offset: next 8-row group
+  d |= (uint64_t)(16u >> 4) << 16;                   // leading byte offset (unused: K fits the swizzle)
+  d |= (uint64_t)((8u * row_bytes) >> 4) << 32;      // stride byte offset: next 8-row group
   d |= (uint64_t)1 << 46;                            // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;                            // layout: 128-byte swizzle
+  d |= (uint64_t)layout << 61;                       // swizzle mode
   return d;
+}
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  return smem_desc_kmajor(saddr, 2u, 128u);
 }
 
 // Instruction descriptor for kind::f16 with fp32 accumulation, both operands K-major.

@@ -6,27 +6,29 @@
 //
 // Shape of the computation: an implicit GEMM whose M dimension is output rows, N is Cout and
 // K is (offset, input channel). A work item is 128 output rows (a tile of `row_order`, which
-// groups rows with equal neighbour masks) x BN output channels. Its K loop visits only the offsets for which at least one of
-// its 128 rows has a neighbour -- the union of the rows' masks -- and within an offset walks
-// Cin in 64-channel stages.
+// groups rows with equal neighbour masks) x BN output channels. Its K loop visits only the
+// offsets for which at least one of its 128 rows has a neighbour -- the union of the rows'
+// masks -- and within an offset walks Cin in BK-channel stages (BK = 64 with the 128-byte
+// swizzle, or 32 with the 64-byte swizzle when Cin is an odd multiple of 32).
 //
 // Persistent CTAs (one per SM) take work items from an atomic counter. Items run one
 // BN-wide slab of output channels at a time (so one slab of weights is live in L2), and within
 // a slab in the order `tile_order` gives the row tiles (most offsets first), so the shortest
-// items come last. Warp roles (352 threads):
-//   warp 0      TMA producer: W[k][kb*64 : +64, n0 : n0+BN] from the spconv (Cout, K*Cin)
-//               matrix, K-major, 128-byte swizzle, one tiled 2-D load per stage;
+// items come last. Warp roles (448 threads):
+//   warp 0      TMA producer: W[k][kb*BK : +BK, n0 : n0+BN] from the spconv (Cout, K*Cin)
+//               matrix, K-major, swizzled, one tiled 2-D load per stage;
 //   warp 1      TMEM allocator (two BN-column accumulators) and the single thread that issues
-//               tcgen05.mma (M=128, N=BN, K=16, four per stage) and tcgen05.commit;
-//   warps 2-5   gatherers: copy each A stage (128 neighbour rows x 128 bytes) with 16-byte
-//               cp.async -- eight threads per row, so a warp instruction reads four whole rows
-//               -- zero-filled for missing neighbours, in the 128-byte swizzle TMA would write;
+//               tcgen05.mma (M=128, N=BN, K=16, BK/16 per stage) and tcgen05.commit;
+//   warps 2-5   gatherers: copy each A stage (128 neighbour rows x 2*BK bytes) with 16-byte
+//               cp.async -- whole rows per group of threads, so a warp instruction reads
+//               complete rows -- zero-filled for missing neighbours, in the swizzled layout TMA
+//               would write;
 //   warps 6-9   epilogue: tcgen05.ld of 32 accumulator columns at a time, + bias, round,
 //               16-byte stores to the row's output; it drains one accumulator while the MMA
 //               fills the other;
-//   warp 10     stager: fetches the next work item and stages its rows and their neighbour
-//               lists (double-buffered) while the current item is gathered.
-// Barriers: a 4-deep (A 16 KB, B BN*128 B) stage ring (full/empty), two accumulator buffers
+//   warps 10-13 stagers: fetch the next work item and stage its rows and their neighbour
+//               lists (one row per thread, double-buffered) while the current item runs.
+// Barriers: a stage ring (full/empty; 4 to 8 deep depending on BN), two accumulator buffers
 // (full/empty) and two work-item slots (full/empty). Every wait is bounded: on expiry the
 // kernel ORs SV_DEVICE_WAIT_TIMEOUT into the status word, all roles unwind, copies drain and
 // TMEM is freed.
@@ -39,11 +41,9 @@ namespace sv {
 namespace {
 
 constexpr int TBM = 128;       // output rows per tile == TMEM lanes
-constexpr int TBK = 64;        // input channels per stage == one 128-byte swizzle row
-constexpr int TSTAGES = 4;
-constexpr int TTHREADS = 352;
+constexpr int TTHREADS = 448;
 constexpr int TMAX_KVOL = 27;
-constexpr int A_STAGE_BYTES = TBM * TBK * 2;
+constexpr int STAGER_BAR = 1;  // named barrier of the four stager warps
 
 struct WorkSlot {
   int32_t item;    // < 0: no more work
@@ -52,21 +52,29 @@ struct WorkSlot {
   int32_t pad;
 };
 
-template <int BN>
+template <int BN, int BK>
 struct TcLayout {
-  static constexpr int B_STAGE_BYTES = BN * TBK * 2;
+  static constexpr int ROW_BYTES = BK * 2;                 // one swizzle row of the A/B tiles
+  static constexpr uint32_t SWIZZLE = BK == 64 ? 2u : 4u;  // descriptor layout: 128 B / 64 B
+  static constexpr int A_STAGE_BYTES = TBM * ROW_BYTES;
+  static constexpr int B_STAGE_BYTES = BN * ROW_BYTES;
+  static constexpr int STAGE_BUDGET = 192 * 1024;
+  static constexpr int STAGES_FIT = STAGE_BUDGET / (A_STAGE_BYTES + B_STAGE_BYTES);
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int A_OFF = 0;
-  static constexpr int B_OFF = TSTAGES * A_STAGE_BYTES;
-  static constexpr int NBR_OFF = B_OFF + TSTAGES * B_STAGE_BYTES;
+  static constexpr int B_OFF = STAGES * A_STAGE_BYTES;
+  static constexpr int NBR_OFF = B_OFF + STAGES * B_STAGE_BYTES;
   static constexpr int OROW_OFF = NBR_OFF + 2 * TBM * TMAX_KVOL * 4;  // nbr [2][128][27]
-  static constexpr int SLOT_OFF = OROW_OFF + 2 * TBM * 4;         // WorkSlot[2]
-  static constexpr int MISC_OFF = SLOT_OFF + 2 * 16;              // tmem, abort
+  static constexpr int SLOT_OFF = OROW_OFF + 2 * TBM * 4;             // orow [2][128]
+  static constexpr int MISC_OFF = SLOT_OFF + 2 * 16;  // tmem, abort, fetch, pad, wmask[4]
   static constexpr int BAR_OFF = MISC_OFF + 32;
-  static constexpr int NUM_BARS = 2 * TSTAGES + 8;
+  static constexpr int NUM_BARS = 2 * STAGES + 8;
   static constexpr int BYTES = BAR_OFF + NUM_BARS * 8;
   static constexpr int SMEM = BYTES + 1024;  // slack for aligning the base to 1024 bytes
   static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static_assert(STAGES >= 4, "pipeline depth");
   static_assert(BAR_OFF % 8 == 0, "mbarriers need 8-byte alignment");
+  static_assert(A_STAGE_BYTES % 1024 == 0 && B_STAGE_BYTES % 1024 == 0, "swizzle atoms");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM columns");
 };
@@ -86,6 +94,21 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Barrier of the 128 stager threads that also ORs a predicate across them, so that all stagers
+// take the same exit decision (one that left alone would leave the others at the barrier).
+__device__ __forceinline__ bool stager_bar_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, %2, 128, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(STAGER_BAR)
+      : "memory");
+  return r != 0;
+}
+
 struct Sched {
   int32_t* counter;           // zeroed before the launch
   const int32_t* tile_order;  // row tiles, most expensive first (nullable: identity)
@@ -103,13 +126,14 @@ __device__ __forceinline__ void decode_item(const Sched& sc, int32_t item, int32
   *n0 = nt * BN;
 }
 
-template <int BN, typename T>
+template <int BN, int BK, typename T>
 __global__ void __launch_bounds__(TTHREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T* __restrict__ feat,
                    int n, int cin, const int32_t* __restrict__ nbr, int kvol,
                    const int32_t* __restrict__ row_order, const T* __restrict__ bias, int cout,
                    T* __restrict__ out, Sched sc, int32_t* status) {
-  using L = TcLayout<BN>;
+  using L = TcLayout<BN, BK>;
+  constexpr int S = L::STAGES;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -121,27 +145,29 @@ __global__ void __launch_bounds__(TTHREADS, 1)
   WorkSlot* slots = reinterpret_cast<WorkSlot*>(smem + L::SLOT_OFF);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+  int32_t* s_fetch = reinterpret_cast<int32_t*>(smem + L::MISC_OFF + 8);
+  uint32_t* s_wmask = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF + 16);  // [4]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* full = bars;                    // [TSTAGES]
-  uint64_t* empty = bars + TSTAGES;         // [TSTAGES]
-  uint64_t* acc_full = bars + 2 * TSTAGES;  // [2]
-  uint64_t* acc_empty = acc_full + 2;       // [2]
-  uint64_t* work_full = acc_empty + 2;      // [2]
-  uint64_t* work_empty = work_full + 2;     // [2]
+  uint64_t* full = bars;                // [S]
+  uint64_t* empty = bars + S;           // [S]
+  uint64_t* acc_full = bars + 2 * S;    // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* work_full = acc_empty + 2;  // [2]
+  uint64_t* work_empty = work_full + 2; // [2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int kb_per_k = cin / TBK;
+  const int kb_per_k = cin / BK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TSTAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1 + TBM);  // TMA expect_tx arrival + 128 cp.async arrivals
       mbar_init(&empty[s], 1);       // tcgen05.commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);      // tcgen05.commit
       mbar_init(&acc_empty[b], TBM);   // every epilogue thread
-      mbar_init(&work_full[b], 1);     // the stager, once the item is staged
+      mbar_init(&work_full[b], 1);     // one stager, once the item is staged
       mbar_init(&work_empty[b], TBM);  // every epilogue thread, once the item is stored
     }
     *s_abort = 0;
@@ -173,14 +199,14 @@ __global__ void __launch_bounds__(TTHREADS, 1)
         for (uint32_t m = w.umask; m != 0 && ok; m &= m - 1) {
           const int k = __ffs(m) - 1;
           for (int kb = 0; kb < kb_per_k; ++kb, ++it) {
-            const int slot = it % TSTAGES;
-            if (!mbar_wait_bounded(&empty[slot], ((it / TSTAGES) & 1) ^ 1, s_abort)) {
+            const int slot = it % S;
+            if (!mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, s_abort)) {
               ok = false;
               break;
             }
             mbar_arrive_expect_tx(&full[slot], L::B_STAGE_BYTES);
             tma_load_2d(smem_u32(sB + slot * L::B_STAGE_BYTES), &tmap_w, &full[slot],
-                        k * cin + kb * TBK, w.n0);
+                        k * cin + kb * BK, w.n0);
           }
         }
       }
@@ -209,18 +235,19 @@ __global__ void __launch_bounds__(TTHREADS, 1)
         int first = 1;
         for (uint32_t m = w.umask; m != 0 && ok; m &= m - 1) {
           for (int kb = 0; kb < kb_per_k; ++kb, ++it) {
-            const int slot = it % TSTAGES;
-            if (!mbar_wait_bounded(&full[slot], (it / TSTAGES) & 1, s_abort)) {
+            const int slot = it % S;
+            if (!mbar_wait_bounded(&full[slot], (it / S) & 1, s_abort)) {
               ok = false;
               break;
             }
             tc_fence_after();
             fence_proxy_async_smem();  // cp.async wrote A through the generic proxy
-            const uint32_t a0 = smem_u32(sA + slot * A_STAGE_BYTES);
+            const uint32_t a0 = smem_u32(sA + slot * L::A_STAGE_BYTES);
             const uint32_t b0 = smem_u32(sB + slot * L::B_STAGE_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < TBK / 16; ++kk)
-              tc_mma_f16(d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+            for (int kk = 0; kk < BK / 16; ++kk)
+              tc_mma_f16(d, smem_desc_kmajor(a0 + kk * 32, L::SWIZZLE, L::ROW_BYTES),
+                         smem_desc_kmajor(b0 + kk * 32, L::SWIZZLE, L::ROW_BYTES), idesc,
                          (first && kk == 0) ? 0u : 1u);
             first = 0;
             tc_commit(&empty[slot]);
@@ -232,10 +259,19 @@ __global__ void __launch_bounds__(TTHREADS, 1)
     }
   } else if (warp < 6) {
     // ---- gatherers ----
+    // CPR 16-byte chunks per row; gatherer g copies chunk g % CPR of tile rows
+    // g / CPR + RPP * i (RPP = 128 / CPR rows per pass, TBM / RPP passes): a warp instruction
+    // moves 32 / CPR whole rows, so every L2 sector it touches is used in full.
+    constexpr int CPR = L::ROW_BYTES / 16;
+    constexpr int RPP = 128 / CPR;
+    constexpr int PASSES = TBM / RPP;
     const int g = threadIdx.x - 64;
-    const uint32_t chunk = g & 7;
-    const int row0 = g >> 3;
-    const uint32_t swz = ((chunk ^ (uint32_t)(row0 & 7)) << 4);  // (row0 + 16*i) & 7 == row0 & 7
+    const uint32_t chunk = g % CPR;
+    const int row0 = g / CPR;
+    // the swizzle XORs the chunk index with address bits above the row: (row & 7) for 128-byte
+    // rows, (row >> 1) & 3 for 64-byte rows; both are the same for all rows row0 + RPP * i
+    const uint32_t swz = BK == 64 ? ((chunk ^ (uint32_t)(row0 & 7)) << 4)
+                                  : ((chunk ^ (uint32_t)((row0 >> 1) & 3)) << 4);
     int it = 0;
     for (int local = 0; ok; ++local) {
       const int ws = local & 1;
@@ -248,25 +284,25 @@ __global__ void __launch_bounds__(TTHREADS, 1)
       const int32_t* nb = s_nbr + ws * TBM * TMAX_KVOL;
       for (uint32_t m = w.umask; m != 0 && ok; m &= m - 1) {
         const int k = __ffs(m) - 1;
-        const T* src[8];
-        uint32_t nbytes[8];
+        const T* src[PASSES];
+        uint32_t nbytes[PASSES];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int32_t s_row = nb[(row0 + 16 * i) * TMAX_KVOL + k];
+        for (int i = 0; i < PASSES; ++i) {
+          const int32_t s_row = nb[(row0 + RPP * i) * TMAX_KVOL + k];
           src[i] = feat + (s_row >= 0 ? (int64_t)s_row * cin : 0) + chunk * 8;
           nbytes[i] = s_row >= 0 ? 16u : 0u;
         }
         for (int kb = 0; kb < kb_per_k; ++kb, ++it) {
-          const int slot = it % TSTAGES;
-          if (!mbar_wait_bounded(&empty[slot], ((it / TSTAGES) & 1) ^ 1, s_abort)) {
+          const int slot = it % S;
+          if (!mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, s_abort)) {
             ok = false;
             break;
           }
-          const uint32_t dst =
-              smem_u32(sA + slot * A_STAGE_BYTES) + (uint32_t)row0 * 128u + swz;
+          const uint32_t dst = smem_u32(sA + slot * L::A_STAGE_BYTES) +
+                               (uint32_t)row0 * (uint32_t)L::ROW_BYTES + swz;
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            cp_async_16(dst + (uint32_t)(16 * i) * 128u, src[i] + kb * TBK, nbytes[i]);
+          for (int i = 0; i < PASSES; ++i)
+            cp_async_16(dst + (uint32_t)(RPP * i * L::ROW_BYTES), src[i] + kb * BK, nbytes[i]);
           cp_async_arrive_noinc(&full[slot]);
         }
       }
@@ -275,66 +311,6 @@ __global__ void __launch_bounds__(TTHREADS, 1)
       cp_async_wait_all();
       report(status, SV_DEVICE_WAIT_TIMEOUT);
     }
-  } else if (warp == 10) {
-    // ---- stager: next work item, its rows and their neighbour lists ----
-    for (int local = 0; ok; ++local) {
-      const int ws = local & 1;
-      int32_t item = 0;
-      if (lane == 0) item = atomicAdd(sc.counter, 1);
-      item = __shfl_sync(0xffffffffu, item, 0);
-      const bool valid = item < sc.total_items;
-      int32_t row_tile = 0, n0 = 0;
-      if (valid) decode_item<BN>(sc, item, &row_tile, &n0);
-      // slot ws (its rows, neighbour lists and accumulator) is free once the epilogue stored
-      // the item two back; that also means the gatherers are done with it
-      if (!__all_sync(0xffffffffu,
-                      mbar_wait_bounded(&work_empty[ws], ((local >> 1) & 1) ^ 1, s_abort))) {
-        ok = false;
-        break;
-      }
-      uint32_t mask = 0;
-      if (valid) {
-        int32_t* nb = s_nbr + ws * TBM * TMAX_KVOL;
-        for (int r = lane; r < TBM; r += 32) {
-          const int64_t gr = (int64_t)row_tile * TBM + r;
-          int32_t orow = -1;
-          if (gr < n) {
-            orow = row_order ? __ldg(&row_order[gr]) : (int32_t)gr;
-            if (orow < 0 || orow >= n) {
-              report(status, SV_DEVICE_BAD_INDEX);
-              orow = -1;
-            }
-          }
-          s_orow[ws * TBM + r] = orow;
-          const int32_t* nrow = nbr + (int64_t)(orow >= 0 ? orow : 0) * kvol;
-#pragma unroll
-          for (int k = 0; k < TMAX_KVOL; ++k) {
-            if (k < kvol) {
-              int32_t v = orow >= 0 ? __ldg(&nrow[k]) : -1;
-              if (v >= n) {
-                report(status, SV_DEVICE_BAD_INDEX);
-                v = -1;
-              }
-              nb[r * TMAX_KVOL + k] = v;
-              mask |= (uint32_t)(v >= 0) << k;
-            }
-          }
-        }
-      }
-      mask = __reduce_or_sync(0xffffffffu, mask);
-      __syncwarp();  // every lane's rows are in shared memory before the item is published
-      if (lane == 0) {
-        WorkSlot w;
-        w.item = valid ? item : -1;
-        w.n0 = n0;
-        w.umask = mask;
-        w.pad = 0;
-        slots[ws] = w;
-        mbar_arrive(&work_full[ws]);
-      }
-      if (!valid) break;
-    }
-    if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
   } else if (warp < 10) {
     // ---- epilogue: warp w may read TMEM lanes 32*(w % 4) .. +31 ----
     const int q = warp & 3;
@@ -391,6 +367,70 @@ __global__ void __launch_bounds__(TTHREADS, 1)
       mbar_arrive(&work_empty[ws]);
     }
     if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
+  } else {
+    // ---- stagers: next work item, its rows and their neighbour lists (one row each) ----
+    const int r = threadIdx.x - 320;
+    for (int local = 0;; ++local) {
+      const int ws = local & 1;
+      if (r == 0) *s_fetch = atomicAdd(sc.counter, 1);
+      // the fetched item is visible, every stager is done with the previous one, and a stager
+      // whose wait expired makes all of them leave together
+      if (stager_bar_any(!ok)) {
+        ok = false;
+        break;
+      }
+      const int32_t item = *s_fetch;
+      const bool valid = item < sc.total_items;
+      int32_t row_tile = 0, n0 = 0;
+      if (valid) decode_item<BN>(sc, item, &row_tile, &n0);
+      // slot ws (rows, neighbour lists and accumulator) is free once the epilogue has stored
+      // the item two back, which also means the gatherers are done with it
+      const bool slot_free =
+          mbar_wait_bounded(&work_empty[ws], ((local >> 1) & 1) ^ 1, s_abort);
+      uint32_t mask = 0;
+      if (valid && slot_free) {
+        const int64_t gr = (int64_t)row_tile * TBM + r;
+        int32_t orow = -1;
+        if (gr < n) {
+          orow = row_order ? __ldg(&row_order[gr]) : (int32_t)gr;
+          if (orow < 0 || orow >= n) {
+            report(status, SV_DEVICE_BAD_INDEX);
+            orow = -1;
+          }
+        }
+        s_orow[ws * TBM + r] = orow;
+        int32_t* nb = s_nbr + ws * TBM * TMAX_KVOL + r * TMAX_KVOL;
+        const int32_t* nrow = nbr + (int64_t)(orow >= 0 ? orow : 0) * kvol;
+#pragma unroll
+        for (int k = 0; k < TMAX_KVOL; ++k) {
+          if (k < kvol) {
+            int32_t v = orow >= 0 ? __ldg(&nrow[k]) : -1;
+            if (v >= n) {
+              report(status, SV_DEVICE_BAD_INDEX);
+              v = -1;
+            }
+            nb[k] = v;
+            mask |= (uint32_t)(v >= 0) << k;
+          }
+        }
+      }
+      mask = __reduce_or_sync(0xffffffffu, mask);
+      if (lane == 0) s_wmask[warp - 10] = mask;
+      // every row is staged; a slot wait that expired anywhere stops all stagers
+      const bool fail = stager_bar_any(!slot_free);
+      if (r == 0) {
+        WorkSlot w;
+        w.item = (valid && !fail) ? item : -1;
+        w.n0 = n0;
+        w.umask = s_wmask[0] | s_wmask[1] | s_wmask[2] | s_wmask[3];
+        w.pad = 0;
+        slots[ws] = w;
+        mbar_arrive(&work_full[ws]);
+      }
+      if (fail) ok = false;
+      if (!valid || fail) break;
+    }
+    if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
   }
 
   tc_fence_before();
@@ -419,36 +459,38 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int weight_map(const ConvArgs& a, bool bf16, int box_rows, CUtensorMap* tmap) {
+// The spconv weight as one (Cout, K*Cin) matrix; box of BK input channels x BN output rows.
+int weight_map(const ConvArgs& a, bool bf16, int box_k, int box_rows, CUtensorMap* tmap) {
   EncodeTiledFn encode = encode_fn();
   if (encode == nullptr) SV_FAIL(SV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t gdim[2] = {(cuuint64_t)a.kvol * a.cin, (cuuint64_t)a.cout};
   const cuuint64_t gstride[1] = {(cuuint64_t)a.kvol * a.cin * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)TBK, (cuuint32_t)box_rows};
+  const cuuint32_t box[2] = {(cuuint32_t)box_k, (cuuint32_t)box_rows};
   const cuuint32_t estride[2] = {1, 1};
   CUresult cr = encode(tmap,
                        bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                        2, const_cast<void*>(a.weight), gdim, gstride, box, estride,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       box_k == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) SV_FAIL(SV_ERR_CUDA, "cuTensorMapEncodeTiled failed for the weight");
   return SV_OK;
 }
 
-template <int BN, typename T>
+template <int BN, int BK, typename T>
 int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
-  using L = TcLayout<BN>;
+  using L = TcLayout<BN, BK>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   int dev = 0;
   SV_CUDA_TRY(cudaGetDevice(&dev));
   static bool attr_done[256] = {};
   if (dev >= 256 || !attr_done[dev]) {
-    SV_CUDA_TRY(cudaFuncSetAttribute(conv_tc_kernel<BN, T>,
+    SV_CUDA_TRY(cudaFuncSetAttribute(conv_tc_kernel<BN, BK, T>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
     if (dev < 256) attr_done[dev] = true;
   }
   CUtensorMap tmap;
-  const int rc = weight_map(a, kBF16, BN, &tmap);
+  const int rc = weight_map(a, kBF16, BK, BN, &tmap);
   if (rc != SV_OK) return rc;
 
   Sched sc;
@@ -461,27 +503,33 @@ int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cu
   const int grid = (int)std::min<int64_t>(items, num_sms());
   sc.total_items = (int32_t)items;
   SV_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int32_t), s));
-  conv_tc_kernel<BN, T><<<grid, TTHREADS, L::SMEM, s>>>(
+  conv_tc_kernel<BN, BK, T><<<grid, TTHREADS, L::SMEM, s>>>(
       tmap, static_cast<const T*>(a.features), (int)a.n, a.cin, a.nbr, a.kvol,
       a.row_order, static_cast<const T*>(a.bias), a.cout, static_cast<T*>(a.out), sc, a.status);
   SV_LAUNCH_CHECK();
   return SV_OK;
 }
 
+template <int BK, typename T>
+int launch_bk(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
+  if (a.cout % 256 == 0) return launch_bn<256, BK, T>(a, tile_order, counter, s);
+  if (a.cout % 128 == 0) return launch_bn<128, BK, T>(a, tile_order, counter, s);
+  if (a.cout % 64 == 0) return launch_bn<64, BK, T>(a, tile_order, counter, s);
+  return launch_bn<32, BK, T>(a, tile_order, counter, s);
+}
+
 template <typename T>
 int launch_typed(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
                  cudaStream_t s) {
-  if (a.cout % 256 == 0) return launch_bn<256, T>(a, tile_order, counter, s);
-  if (a.cout % 128 == 0) return launch_bn<128, T>(a, tile_order, counter, s);
-  if (a.cout % 64 == 0) return launch_bn<64, T>(a, tile_order, counter, s);
-  return launch_bn<32, T>(a, tile_order, counter, s);
+  if (a.cin % 64 == 0) return launch_bk<64, T>(a, tile_order, counter, s);
+  return launch_bk<32, T>(a, tile_order, counter, s);
 }
 
 }  // namespace
 
 bool conv_tc_supported(const ConvArgs& a) {
   return (a.dtype == SV_FLOAT16 || a.dtype == SV_BFLOAT16) && a.layout == SV_WEIGHT_OKI &&
-         a.cin > 0 && a.cin % TBK == 0 && a.cout > 0 && a.cout % 32 == 0 && a.kvol >= 1 &&
+         a.cin > 0 && a.cin % 32 == 0 && a.cout > 0 && a.cout % 32 == 0 && a.kvol >= 1 &&
          a.kvol <= TMAX_KVOL && a.n <= INT32_MAX - TBM && (int64_t)a.kvol * a.cin < INT32_MAX &&
          aligned16(a.features) && aligned16(a.weight) && aligned16(a.out);
 }

@@ -96,7 +96,9 @@ def test_conv_half_matches_fp32_reference(golden, dtype, algo):
 
 @pytest.mark.parametrize(
     "cin,cout",
-    [(64, 32), (64, 64), (128, 128), (64, 256), (192, 512), (1024, 1024), (256, 96)],
+    [(64, 32), (64, 64), (128, 128), (64, 256), (192, 512), (1024, 1024), (256, 96),
+     # Cin an odd multiple of 32: 32-channel K stages with the 64-byte swizzle
+     (32, 32), (32, 128), (96, 64), (160, 256)],
 )
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_tcgen05_shapes(cin, cout, dtype):
@@ -112,15 +114,15 @@ def test_tcgen05_shapes(cin, cout, dtype):
     assert max_rel_err(out, ref) <= HALF_TOL
 
 
-@pytest.mark.parametrize("cout", [64, 128, 256])
-def test_tcgen05_persistent_ctas_take_several_items(cout):
+@pytest.mark.parametrize("cin,cout", [(64, 64), (64, 128), (64, 256), (32, 32), (32, 256)])
+def test_tcgen05_persistent_ctas_take_several_items(cin, cout):
     """24k rows give more work items than SMs, so each persistent CTA runs several items and
     reuses both accumulator buffers and both work slots; every item must match the reference."""
 
     coords = scenes.shell32_batch(4)
     dtype = torch.bfloat16
-    f = _rounded(scenes.normal_features(len(coords), 64, seed=31), dtype)
-    w = _rounded(scenes.conv_weight(cout, 64, 3, seed=32), dtype)
+    f = _rounded(scenes.normal_features(len(coords), cin, seed=31), dtype)
+    w = _rounded(scenes.conv_weight(cout, cin, 3, seed=32), dtype)
     b = _rounded(np.random.default_rng(33).standard_normal(cout).astype(np.float32), dtype)
     ref = O.sparse_conv3d(f, O.build_neighbor_map(coords, 3), O.spconv_weight_to_kio(w), b)
     out, _ = _run(coords, f, w, b, dtype, algo=N.SV_CONV_TCGEN05)
