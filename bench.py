@@ -45,13 +45,16 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument(
         "--workload",
-        choices=["conv1024", "kmap", "pool", "scene128", "sweep"],
+        choices=["conv1024", "kmap", "pool", "scene128", "sweep", "halo", "topology"],
         default="conv1024",
         help="conv1024 (default): the headline line above. The others run on one GPU and "
         "print one line each: kmap = kernel-map build on 16 x 128^3 at 8%% occupancy; pool = "
         "downsample + upsample of the 237k-voxel 128^3 scene at 128 channels; scene128 = "
         "convs 64->64->32 on that scene; sweep = map build and conv over occupancy "
-        "{0.5, 2, 8, 30}%% x grid {64, 128}^3 x width {32, 128, 512, 1024}, batch 16",
+        "{0.5, 2, 8, 30}%% x grid {64, 128}^3 x width {32, 128, 512, 1024}, batch 16; halo = "
+        "the 128^3 scene Morton-partitioned over the torchrun ranks (strong scaling), convs "
+        "64->64->32 each after an NCCL halo exchange; topology = occupancy -> coords on 16 x 64^3 "
+        "logits, sparse_subdivide and 8^3 attention windows of the 128^3 scene",
     )
     p.add_argument(
         "--profiling",
@@ -461,7 +464,7 @@ def run_ours(args) -> None:
             },
             "roofline": {
                 "bound": "tensor",
-                "kernel": "conv_tc_kernel<256, bf16>",
+                "kernel": "conv_tc_kernel<256, 64, bf16>",
                 "achieved": achieved,
                 "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s",
@@ -638,15 +641,163 @@ def run_workload(args) -> None:
                         {"workload": f"uniform{grid}x16_{occ:g}_c{ch}_bf16",
                          "voxels": len(coords), "valid_pairs": pairs, "kmap_ms": ms_map,
                          "kmap_roofline": roof_map}, roof))
+    elif args.workload == "topology":
+        from mlx_diffuser_b200.layers.sparse import attention_windows, occupied_coordinates, sparse_subdivide
+
+        rng = np.random.default_rng(3)
+        logits = torch.from_numpy(rng.standard_normal((16, 64, 64, 64)).astype(np.float32) - 1.6)
+        logits = logits.to(dev)
+        m = occupied_coordinates(logits, 0.0).shape[0]
+        ms = _time_device(lambda: occupied_coordinates(logits, 0.0), args.steps, args.warmup,
+                          flush)
+        cells = logits.numel()
+        lines.append(_line("occupancy cells/s", cells / (ms * 1e-3), "cells/s", ms, args,
+                           {"workload": "occupancy_16x64^3_f32", "cells": cells, "occupied": m},
+                           _hbm_roofline(4.0 * cells + 16.0 * m, ms,
+                                         "occ_count_kernel + occ_emit_kernel")))
+        coords = scenes.scene128(0)
+        n = len(coords)
+        x = SparseTensor(torch.from_numpy(scenes.normal_features(n, 64, 3)).to(dev, torch.bfloat16),
+                         torch.from_numpy(coords).to(dev))
+        ms = _time_device(lambda: sparse_subdivide(x), args.steps, args.warmup, flush)
+        lines.append(_line("sparse_subdivide voxels/s", n / (ms * 1e-3), "voxels/s", ms, args,
+                           {"workload": "scene128_subdivide_c64_bf16", "voxels": n},
+                           _hbm_roofline(16.0 * n + 128.0 * n + 8 * (16.0 * n + 128.0 * n), ms,
+                                         "subdivide_coords_kernel + expand_rows_kernel")))
+
+        def windows():
+            x.cache.clear()
+            return attention_windows(x, 8, (4, 4, 4))
+
+        groups = windows().num_groups
+        ms = _time_device(windows, args.steps, args.warmup, flush)
+        lines.append(_line("attention windows voxels/s", n / (ms * 1e-3), "voxels/s", ms, args,
+                           {"workload": "scene128_windows8_shift4", "voxels": n,
+                            "groups": groups},
+                           _hbm_roofline(16.0 * n + 4.0 * n + 4.0 * (groups + 1), ms,
+                                         "window grouping (key sort + first-row sort)")))
     for line in lines:
         print(json.dumps(line), flush=True)
     N.check_device_status(dev)
+
+
+def run_halo(args) -> None:
+    """One 128^3 scene (237k voxels) split over the ranks by Morton range. A step is what two
+    stacked ``SparseConv3D`` layers (64->64, 64->32, bf16) need on a partitioned scene: halo
+    exchange of the layer's input rows (NCCL send/recv), then the local tensor-core conv whose
+    output buffer is the next layer's local buffer. The plan and the local maps are built once,
+    like the reference's cached neighbour map. Strong scaling: total work is fixed."""
+
+    import torch
+    import torch.distributed as dist
+
+    from mlx_diffuser_b200 import _native as N
+    from mlx_diffuser_b200 import scenes
+    from mlx_diffuser_b200.distributed import HaloPlan, gather_rows
+    from mlx_diffuser_b200.kernels.sparse import conv3d_forward
+    from mlx_diffuser_b200.layers.sparse import build_neighbor_map, conv_row_order
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    coords_np = scenes.scene128(0)
+    n = len(coords_np)
+    coords = torch.from_numpy(coords_np).to(dev)
+    nbr = build_neighbor_map(coords, 3)
+    plan = HaloPlan.build(coords, nbr, rank, world)
+    lnbr = plan.local_nbr.to(dev)
+    row_order, tile_order = conv_row_order(lnbr)
+    dt = torch.bfloat16
+    w1 = torch.from_numpy(scenes.conv_weight(64, 64, 3, 41)).to(dev, dt).contiguous()
+    w2 = torch.from_numpy(scenes.conv_weight(32, 64, 3, 42)).to(dev, dt).contiguous()
+    b1 = torch.zeros(64, device=dev, dtype=dt)
+    b2 = torch.zeros(32, device=dev, dtype=dt)
+    feats = torch.from_numpy(scenes.normal_features(n, 64, 40)).to(dev, dt)
+    x_local = torch.zeros((plan.num_local, 64), device=dev, dtype=dt)
+    x_local[: plan.num_own] = feats[plan.own]
+    h_local = torch.empty((plan.num_local, 64), device=dev, dtype=dt)
+    y_local = torch.empty((plan.num_local, 32), device=dev, dtype=dt)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        plan.exchange(x_local, gather=gather_rows)
+        conv3d_forward(x_local, lnbr, w1, N.SV_WEIGHT_OKI, b1, 64, row_order=row_order,
+                       tile_order=tile_order, out=h_local)
+        plan.exchange(h_local, gather=gather_rows)
+        conv3d_forward(h_local, lnbr, w2, N.SV_WEIGHT_OKI, b2, 32, row_order=row_order,
+                       tile_order=tile_order, out=y_local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    barrier()
+    N.check_device_status(dev)
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    barrier()
+    sampler.start()
+    for a, b in events:
+        flush.fill_(1.0)
+        a.record()
+        step()
+        b.record()
+    barrier()
+    clocks = sampler.stop()
+    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in events) / args.steps],
+                      dtype=torch.float64, device=dev)
+    halo = torch.tensor([float(plan.halo.numel())], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(halo)
+    ms_v, halo_v = float(ms.item()), float(halo.item())
+    if rank == 0:
+        pairs = int((nbr >= 0).sum().item())
+        print(json.dumps({
+            "metric": "sparse conv3d active-voxels/s (2 stacked layers, one partitioned scene)",
+            "value": n / (ms_v * 1e-3),
+            "unit": "voxels/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_v,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": "scene128_halo_conv64to64to32_bf16",
+                "voxels": n,
+                "valid_pairs": pairs,
+                "halo_rows_total": int(halo_v),
+                "halo_fraction": halo_v / n,
+                "parallelism": f"morton-range x{world}",
+                "l2": "flushed between steps (256 MiB write outside the timed events)",
+            },
+            "clocks": clocks,
+        }), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
 
 
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "halo":
+        run_halo(args)
     elif args.workload != "conv1024":
         run_workload(args)
     else:

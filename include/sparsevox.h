@@ -15,6 +15,9 @@
  *   src/mlx_diffuser/kernels/sparse.py:58-105   sparse_conv3d (+ the Metal kernel :9-36)
  *   src/mlx_diffuser/layers/sparse.py:245-284   sparse_downsample
  *   src/mlx_diffuser/layers/sparse.py:287-295   sparse_upsample
+ *   src/mlx_diffuser/layers/sparse.py:298-318   sparse_subdivide
+ *   src/mlx_diffuser/layers/sparse.py:321-342   _attention_groups (sparse_self_attention)
+ *   src/mlx_diffuser/models/trellis.py:278-285  occupied_coordinates (np.argwhere step)
  */
 #ifndef SPARSEVOX_H_
 #define SPARSEVOX_H_
@@ -166,6 +169,50 @@ SV_API int sv_downsample_features(const void* features, int64_t n, int channels,
 SV_API int sv_upsample_features(const void* coarse, int64_t m, int channels, int dtype,
                                 const int32_t* inverse, int64_t n, void* out, int32_t* status,
                                 sv_stream_t stream);
+
+/* ---- topology: occupancy -> coordinates, subdivision, attention windows --------------- */
+
+/* Coordinates of the cells of a [B, D, H, W] logits grid (element strides `strides`, so a
+ * [..., 0] view of a channels-last tensor works) whose value is above `threshold`, as
+ * np.argwhere(logits > threshold) lists them (src/mlx_diffuser/models/trellis.py:278-285):
+ * (b, d, h, w) int32 rows in row-major order. The threshold is rounded to float32 and then to
+ * the logits' dtype before the comparison; NaN is never above it. Two calls on one workspace
+ * (sv_occupancy_workspace_bytes(shape) bytes):
+ *   sv_occupancy_count writes the number of rows m to *out_m (host memory; synchronises
+ *     `stream`) and leaves per-tile offsets in the workspace;
+ *   sv_occupancy_emit then writes the m rows to out_coords ([m, 4], 16-byte aligned), with the
+ *     same logits, shape, strides and threshold. Rows past m (logits changed in between) are
+ *     dropped and SV_DEVICE_BAD_INDEX is ORed into `status`.
+ * Grids of up to 2^31 - 1025 cells. */
+SV_API size_t sv_occupancy_workspace_bytes(const int64_t shape[4]);
+SV_API int sv_occupancy_count(const void* logits, int dtype, const int64_t shape[4],
+                              const int64_t strides[4], double threshold, int64_t* out_m,
+                              void* workspace, size_t workspace_bytes, sv_stream_t stream);
+SV_API int sv_occupancy_emit(const void* logits, int dtype, const int64_t shape[4],
+                             const int64_t strides[4], double threshold, int32_t* out_coords,
+                             int64_t m, int32_t* status, void* workspace, size_t workspace_bytes,
+                             sv_stream_t stream);
+
+/* sparse_subdivide (src/mlx_diffuser/layers/sparse.py:298-318): row i becomes rows 8i + j,
+ * j = 4z + 2y + x, with coordinates (b, 2*c1 + z, 2*c2 + y, 2*c3 + x) (int32, wrapping) and a
+ * copy of feature row i (row_bytes bytes; features may be null when row_bytes == 0).
+ * out_coords [8n, 4], out_features [8n, row_bytes]. */
+SV_API int sv_subdivide(const int32_t* coords, int64_t n, const void* features,
+                        int64_t row_bytes, int32_t* out_coords, void* out_features,
+                        sv_stream_t stream);
+
+/* Attention windows, _attention_groups (src/mlx_diffuser/layers/sparse.py:321-342): rows are
+ * grouped by (b, (c1 + shift[0]) // window, (c2 + shift[1]) // window, (c3 + shift[2]) // window)
+ * (int32 wrapping addition, floor division), or by b alone when window == 0 (the reference's
+ * window_size=None). Groups are listed in the order of their first row, each group's rows
+ * ascending -- the order of the reference's dict of lists. perm [n]: the rows, group after
+ * group; offsets [G + 1] (allocate n + 1): group g is perm[offsets[g] : offsets[g + 1]].
+ * The group count G is written to *out_groups (host memory); this call synchronises `stream`.
+ * Workspace: sv_window_groups_workspace_bytes(n). */
+SV_API size_t sv_window_groups_workspace_bytes(int64_t n);
+SV_API int sv_window_groups(const int32_t* coords, int64_t n, int window, const int32_t shift[3],
+                            int32_t* perm, int32_t* offsets, int64_t* out_groups,
+                            void* workspace, size_t workspace_bytes, sv_stream_t stream);
 
 #ifdef __cplusplus
 }

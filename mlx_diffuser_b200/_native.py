@@ -64,6 +64,12 @@ _SIGNATURES = {
     "sv_downsample_coords": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "sv_downsample_features": (_I32, [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P]),
     "sv_upsample_features": (_I32, [_P, _I64, _I32, _I32, _P, _I64, _P, _P, _P]),
+    "sv_occupancy_workspace_bytes": (_SZ, [_P]),
+    "sv_occupancy_count": (_I32, [_P, _I32, _P, _P, ctypes.c_double, _P, _P, _SZ, _P]),
+    "sv_occupancy_emit": (_I32, [_P, _I32, _P, _P, ctypes.c_double, _P, _I64, _P, _P, _SZ, _P]),
+    "sv_subdivide": (_I32, [_P, _I64, _P, _I64, _P, _P, _P]),
+    "sv_window_groups_workspace_bytes": (_SZ, [_I64]),
+    "sv_window_groups": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _P, _SZ, _P]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -1,9 +1,11 @@
 """Sparse voxel tensors and the TRELLIS sparse conv / pooling primitives, on sm_100a.
 
-Drop-in for the sparse-voxel path of ``mlx_diffuser.layers.sparse``
-(``src/mlx_diffuser/layers/sparse.py:23-295``): ``SparseTensor``, ``build_neighbor_map``,
-``SparseConv3D``, ``sparse_downsample`` and ``sparse_upsample`` keep the reference's names,
-arguments, cache keys and errors. Features and coordinates are CUDA ``torch.Tensor``s (any
+Drop-in for ``mlx_diffuser.layers.sparse`` (``src/mlx_diffuser/layers/sparse.py``):
+``SparseTensor``, ``build_neighbor_map``, ``SparseConv3D``, ``sparse_downsample``,
+``sparse_upsample``, ``sparse_subdivide``, ``sparse_self_attention`` and
+``sparse_cross_attention`` keep the reference's names, arguments, cache keys and errors;
+``occupied_coordinates`` is the argwhere step of the structure decoder
+(``src/mlx_diffuser/models/trellis.py:278-285``). Features and coordinates are CUDA ``torch.Tensor``s (any
 DLPack array is borrowed); every topology and feature computation runs in ``libsparsevox.so``.
 
 Differences that are deliberate:
@@ -423,10 +425,213 @@ def sparse_upsample(x: SparseTensor, factor: int = 2) -> SparseTensor:
     return SparseTensor(features, coords, x.batch_size, spatial_shape, scale, x.cache)
 
 
+def sparse_subdivide(x: SparseTensor) -> SparseTensor:
+    """Replace every occupied voxel with its eight children
+    (``src/mlx_diffuser/layers/sparse.py:298-318``): row i becomes rows 8i + j, j = 4z + 2y + x,
+    at ``(b, 2*c1 + z, 2*c2 + y, 2*c3 + x)`` with a copy of the parent's features. The spatial
+    shape doubles, the scale halves (at least 1), and the result starts with an empty cache
+    (the parent's maps have other row counts)."""
+
+    coords = x.coords.contiguous()
+    N.require_cuda(coords, "coords")
+    dev = coords.device
+    n = coords.shape[0]
+    feats = x.features
+    trailing = feats.shape[1:]
+    flat = feats.reshape(n, math.prod(trailing)).contiguous()
+    out_coords = torch.empty((n * 8, 4), dtype=torch.int32, device=dev)
+    out_feats = torch.empty((n * 8, flat.shape[1]), dtype=flat.dtype, device=dev)
+    row_bytes = flat.shape[1] * flat.element_size()
+    rc = N.load().sv_subdivide(
+        coords.data_ptr(), n, flat.data_ptr() if row_bytes else None, row_bytes,
+        out_coords.data_ptr(), out_feats.data_ptr() if row_bytes else None, N.stream(dev),
+    )
+    N.check(rc, "sparse_subdivide")
+    source_shape = x.spatial_shape or (0, 0, 0)
+    spatial_shape = (source_shape[0] * 2, source_shape[1] * 2, source_shape[2] * 2)
+    scale = (max(x.scale[0] // 2, 1), max(x.scale[1] // 2, 1), max(x.scale[2] // 2, 1))
+    return SparseTensor(out_feats.reshape(n * 8, *trailing), out_coords, x.batch_size,
+                        spatial_shape, scale, {})
+
+
+@dataclasses.dataclass
+class WindowGroups:
+    """Attention windows of a sparse tensor as one device permutation: group g is
+    ``perm[offsets[g]:offsets[g + 1]]``. Groups are in the order of their first row and rows
+    ascend inside a group, the order of the reference's ``_attention_groups`` lists.
+    ``buckets`` maps a group length L to the [groups, L] row-index matrix of all groups of that
+    length (built on first use; one host read of the lengths)."""
+
+    perm: torch.Tensor
+    offsets: torch.Tensor
+    buckets: dict[int, torch.Tensor] | None = None
+
+    @property
+    def num_groups(self) -> int:
+        return int(self.offsets.numel()) - 1
+
+    def as_list(self) -> list[torch.Tensor]:
+        bounds = self.offsets.cpu().tolist()
+        return [self.perm[a:b] for a, b in zip(bounds[:-1], bounds[1:])]
+
+    def by_length(self) -> dict[int, torch.Tensor]:
+        if self.buckets is None:
+            starts = self.offsets[:-1]
+            lengths = self.offsets[1:] - starts
+            buckets: dict[int, torch.Tensor] = {}
+            host = lengths.cpu()
+            for length in dict.fromkeys(host.tolist()):
+                sel = starts[(lengths == length)].long()
+                idx = sel[:, None] + torch.arange(length, device=sel.device)[None]
+                buckets[int(length)] = self.perm[idx].long()
+            self.buckets = buckets
+        return self.buckets
+
+
+def attention_windows(
+    x: SparseTensor, window_size: int | None, shift_window=(0, 0, 0)
+) -> WindowGroups:
+    """Group rows by batch, or by batch and ``(coords + shift) // window_size``, on the GPU
+    (``_attention_groups``, ``src/mlx_diffuser/layers/sparse.py:321-342``), cached under the
+    reference's key ``attention_groups_{window_size}_{shift}_{scale}``."""
+
+    shift = tuple(int(v) for v in shift_window)
+    key = f"attention_groups_{window_size}_{shift}_{x.scale}"
+    cached = x.cache.get(key)
+    if cached is not None:
+        return cached
+    if window_size is not None and int(window_size) < 1:
+        raise ValueError("window_size must be a positive integer or None")
+    if len(shift) != 3:
+        raise ValueError("shift_window must have three entries")
+    coords = x.coords.contiguous()
+    N.require_cuda(coords, "coords")
+    dev = coords.device
+    n = coords.shape[0]
+    perm = torch.empty(n, dtype=torch.int32, device=dev)
+    offsets = torch.zeros(n + 1, dtype=torch.int32, device=dev)
+    groups = ctypes.c_int64(0)
+    lib = N.load()
+    ws_bytes = lib.sv_window_groups_workspace_bytes(n)
+    ws = N.workspace(ws_bytes, dev)
+    rc = lib.sv_window_groups(
+        coords.data_ptr(), n, 0 if window_size is None else int(window_size),
+        (ctypes.c_int * 3)(*shift), perm.data_ptr(), offsets.data_ptr(), ctypes.byref(groups),
+        ws.data_ptr(), ws_bytes, N.stream(dev),
+    )
+    N.check(rc, "attention groups")
+    result = WindowGroups(perm, offsets[: int(groups.value) + 1])
+    x.cache[key] = result
+    return result
+
+
+def _attention_groups(
+    x: SparseTensor, window_size: int | None, shift_window=(0, 0, 0)
+) -> list[torch.Tensor]:
+    """The reference's list-of-index-arrays form of :func:`attention_windows`."""
+
+    return attention_windows(x, window_size, shift_window).as_list()
+
+
+def sparse_self_attention(
+    x: SparseTensor,
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    window_size: int | None = None,
+    shift_window=(0, 0, 0),
+) -> torch.Tensor:
+    """SDPA over each sparse batch or coordinate window
+    (``src/mlx_diffuser/layers/sparse.py:343-377``). ``q``, ``k``, ``v``: ``(N, heads,
+    head_dim)``. Windows of equal occupancy share one attention call, as in the reference; the
+    grouping is the library's, the attention itself is torch's SDPA."""
+
+    if q.shape != k.shape or q.shape != v.shape or q.shape[0] != x.num_points:
+        raise ValueError("q, k, and v must share shape (N, heads, head_dim)")
+    groups = attention_windows(x, window_size, shift_window)
+    out = torch.zeros_like(v)
+    scale = q.shape[-1] ** -0.5
+    for length, idx in groups.by_length().items():
+        qg = q[idx].transpose(1, 2)
+        kg = k[idx].transpose(1, 2)
+        vg = v[idx].transpose(1, 2)
+        attended = torch.nn.functional.scaled_dot_product_attention(qg, kg, vg, scale=scale)
+        attended = attended.transpose(1, 2).reshape(idx.numel(), *q.shape[1:])
+        out.index_add_(0, idx.reshape(-1), attended)
+    return out
+
+
+def sparse_cross_attention(
+    x: SparseTensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor
+) -> torch.Tensor:
+    """Cross-attend sparse point queries to one dense context sequence per batch element
+    (``src/mlx_diffuser/layers/sparse.py:380-407``)."""
+
+    if q.ndim != 3 or q.shape[0] != x.num_points:
+        raise ValueError("q must have shape (N, heads, head_dim)")
+    if k.shape != v.shape or k.ndim != 4 or k.shape[0] != x.batch_size:
+        raise ValueError("k and v must have shape (B, tokens, heads, head_dim)")
+    if q.shape[1:] != k.shape[2:]:
+        raise ValueError("query and context head dimensions must match")
+    out = torch.zeros_like(q)
+    scale = q.shape[-1] ** -0.5
+    for batch, layout in enumerate(x.batch_layout()):
+        if layout.start == layout.stop:
+            continue
+        qb = q[layout][None].transpose(1, 2)
+        kb = k[batch : batch + 1].transpose(1, 2)
+        vb = v[batch : batch + 1].transpose(1, 2)
+        attended = torch.nn.functional.scaled_dot_product_attention(qb, kb, vb, scale=scale)
+        out[layout] += attended[0].transpose(0, 1)
+    return out
+
+
+def occupied_coordinates(logits: torch.Tensor, threshold: float = 0.0) -> torch.Tensor:
+    """``(batch, x, y, z)`` int32 coordinates of the cells whose occupancy logit is above
+    ``threshold``, in ``np.argwhere`` order: the compaction step of
+    ``TrellisSparseStructureDecoder.occupied_coordinates``
+    (``src/mlx_diffuser/models/trellis.py:278-285``), on the GPU. ``logits`` is the decoder's
+    ``(B, D, H, W, C)`` output (channel 0 is used, as the reference's ``[..., 0]``) or a
+    ``(B, D, H, W)`` grid; strided views are read in place."""
+
+    t = N.as_tensor(logits)
+    N.require_cuda(t, "logits")
+    if t.ndim == 5:
+        t = t[..., 0]
+    if t.ndim != 4:
+        raise ValueError(f"occupancy logits must have shape (B, D, H, W[, C]), got {tuple(t.shape)}")
+    if t.dtype not in N.DTYPE_CODE:
+        t = t.to(torch.float32)
+    dev = t.device
+    shape = (ctypes.c_int64 * 4)(*t.shape)
+    strides = (ctypes.c_int64 * 4)(*t.stride())
+    lib = N.load()
+    ws_bytes = lib.sv_occupancy_workspace_bytes(shape)
+    ws = N.workspace(ws_bytes, dev)
+    m = ctypes.c_int64(0)
+    code = N.DTYPE_CODE[t.dtype]
+    rc = lib.sv_occupancy_count(t.data_ptr(), code, shape, strides, float(threshold),
+                                ctypes.byref(m), ws.data_ptr(), ws_bytes, N.stream(dev))
+    N.check(rc, "occupied_coordinates")
+    out = torch.empty((int(m.value), 4), dtype=torch.int32, device=dev)
+    rc = lib.sv_occupancy_emit(t.data_ptr(), code, shape, strides, float(threshold),
+                               out.data_ptr(), out.shape[0], N.status_word(dev).data_ptr(),
+                               ws.data_ptr(), ws_bytes, N.stream(dev))
+    N.check(rc, "occupied_coordinates")
+    return out
+
+
 __all__ = [
     "SparseConv3D",
     "SparseTensor",
+    "WindowGroups",
+    "attention_windows",
     "build_neighbor_map",
+    "occupied_coordinates",
+    "sparse_cross_attention",
     "sparse_downsample",
+    "sparse_self_attention",
+    "sparse_subdivide",
     "sparse_upsample",
 ]

@@ -16,6 +16,9 @@ Covered surface (each item is what those two reference files call):
 * ``random.uniform / random.normal / random.seed``;
 * ``fast.metal_kernel`` -- returns a callable that raises, so only the reference's pure
   fallback (``use_metal=False``) can run;
+* ``fast.scaled_dot_product_attention`` -- a float64 softmax attention, for the reference's
+  ``sparse_self_attention`` / ``sparse_cross_attention``;
+* ``arange``;
 * ``nn.Module`` with ``training`` / ``eval()`` / ``train()``.
 """
 
@@ -118,6 +121,10 @@ def allclose(a, b, rtol=1e-5, atol=1e-8):
     return bool(np.allclose(np.asarray(a), np.asarray(b), rtol=rtol, atol=atol))
 
 
+def arange(start, stop=None, step=1, dtype=None):
+    return _wrap(np.arange(start, stop, step, dtype=dtype))
+
+
 def eval(*_args):  # noqa: A001 - mirrors ``mx.eval``
     return None
 
@@ -150,6 +157,20 @@ class _Fast(types.ModuleType):
             raise RuntimeError("Metal kernels cannot run under the NumPy shim")
 
         return _unavailable
+
+    @staticmethod
+    def scaled_dot_product_attention(q, k, v, *, scale, mask=None):
+        """softmax(q k^T * scale) v over the last two axes of (B, heads, L, D) arrays, in
+        float64 and returned in q's dtype."""
+
+        if mask is not None:
+            raise NotImplementedError("masks are not used by the sparse path")
+        q64, k64, v64 = (np.asarray(t, np.float64) for t in (q, k, v))
+        s = np.einsum("bhld,bhmd->bhlm", q64, k64) * scale
+        s = s - s.max(axis=-1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=-1, keepdims=True)
+        return _wrap(np.einsum("bhlm,bhmd->bhld", p, v64).astype(np.asarray(q).dtype))
 
 
 fast = _Fast()

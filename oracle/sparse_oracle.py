@@ -246,3 +246,67 @@ def sparse_conv3d_fallback_literal(features, neighbors, weights, bias) -> np.nda
         contribution = f[safe_index] @ w[k]
         out = out + contribution * valid[:, None]
     return out
+
+
+# --------------------------------------------------------------------------------------------
+# topology: subdivision, attention windows, occupancy -> coordinates
+# --------------------------------------------------------------------------------------------
+
+
+def subdivide(coords, features) -> tuple[np.ndarray, np.ndarray]:
+    """``sparse_subdivide`` (``src/mlx_diffuser/layers/sparse.py:298-318``): row i becomes rows
+    8i + j, j = 4z + 2y + x in the nested order of the reference's offset list, at
+    (b, 2*c1 + z, 2*c2 + y, 2*c3 + x), each with a copy of feature row i."""
+
+    coords = np.asarray(coords, np.int32)
+    n = len(coords)
+    child = np.array([[0, z, y, x] for z in range(2) for y in range(2) for x in range(2)],
+                     np.int32)
+    scaled = coords[:, None, :] * np.array([1, 2, 2, 2], np.int32)
+    out_coords = (scaled + child[None]).reshape(n * 8, 4)
+    features = np.asarray(features)
+    out_features = np.repeat(features, 8, axis=0)
+    return out_coords, out_features
+
+
+def attention_groups(coords, window_size, shift_window=(0, 0, 0)) -> list[np.ndarray]:
+    """``_attention_groups`` (``src/mlx_diffuser/layers/sparse.py:321-342``): rows grouped by
+    (b) or by (b, (xyz + shift) // window); groups in the order their first row appears, rows
+    ascending inside a group (a dict of lists filled in row order)."""
+
+    coords = np.asarray(coords, np.int32)
+    if window_size is None:
+        keys = coords[:, :1]
+    else:
+        shift = np.asarray(shift_window, dtype=np.int32)
+        keys = np.concatenate([coords[:, :1], (coords[:, 1:] + shift) // window_size], axis=1)
+    groups: dict[tuple[int, ...], list[int]] = {}
+    for index, key in enumerate(keys):
+        groups.setdefault(tuple(int(v) for v in key), []).append(index)
+    return [np.asarray(rows, dtype=np.int32) for rows in groups.values()]
+
+
+def occupied_coordinates(logits, threshold: float = 0.0, dtype: str = "float32") -> np.ndarray:
+    """The ``np.argwhere(logits > threshold)`` step of ``occupied_coordinates``
+    (``src/mlx_diffuser/models/trellis.py:278-285``) on a [B, D, H, W] grid whose values are
+    exact in ``dtype`` ("float32", "float16" or "bfloat16"; given as float32 arrays). The
+    threshold is rounded to float32 and then to ``dtype``, as MLX's promotion of a Python float
+    scalar does, and the comparison of two values exact in ``dtype`` is made in float32."""
+
+    logits = np.asarray(logits, np.float32)
+    thr = np.float32(threshold)
+    if dtype == "float16":
+        thr = np.float32(np.float16(thr))
+    elif dtype == "bfloat16":
+        thr = round_to_bf16(np.array([thr], np.float32))[0]
+    return np.argwhere(logits > thr).astype(np.int32)
+
+
+def round_to_bf16(values) -> np.ndarray:
+    """float32 values rounded to the nearest bfloat16 (ties to even), returned as float32."""
+
+    v = np.ascontiguousarray(np.asarray(values, np.float32))
+    bits = v.view(np.uint32).astype(np.uint64)
+    rounded = (bits + 0x7FFF + ((bits >> 16) & 1)) & 0xFFFF0000
+    out = rounded.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(v), v, out)

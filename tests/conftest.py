@@ -20,10 +20,15 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 
 
+TOPOLOGY = "topology"  # subdivide / attention windows / occupancy fixture, not a conv case
+
+
 def golden_names() -> list[str]:
-    return sorted(
-        os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz"))
-    )
+    """The conv / map / pool fixtures (one input scene each)."""
+
+    names = (os.path.splitext(os.path.basename(p))[0]
+             for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+    return sorted(n for n in names if n != TOPOLOGY)
 
 
 def load_golden(name: str) -> dict[str, np.ndarray]:
@@ -34,3 +39,8 @@ def load_golden(name: str) -> dict[str, np.ndarray]:
 @pytest.fixture(params=golden_names())
 def golden(request):
     return request.param, load_golden(request.param)
+
+
+@pytest.fixture(scope="session")
+def topology_golden():
+    return load_golden(TOPOLOGY)

@@ -7,13 +7,19 @@ Run from the repository root, with the mlx_diffuser sources available:
 MLX cannot be installed here, so the reference files ``src/mlx_diffuser/kernels/sparse.py``
 and ``src/mlx_diffuser/layers/sparse.py`` are executed unmodified on top of the NumPy stand-in
 ``oracle/mlx_shim.py``: ``build_neighbor_map``, ``SparseConv3D`` (its pure fallback,
-``use_metal=False``), ``sparse_downsample`` and ``sparse_upsample``. Their outputs are written
-to ``tests/golden/*.npz``. The fixtures travel with the repository; the reference does not.
+``use_metal=False``), ``sparse_downsample``, ``sparse_upsample``, ``sparse_subdivide``,
+``_attention_groups``, ``sparse_self_attention`` and ``sparse_cross_attention``. The
+occupancy step ``TrellisSparseStructureDecoder.occupied_coordinates``
+(``src/mlx_diffuser/models/trellis.py:278-285``) is taken out of its file by ``ast`` and run as
+written, with a stand-in ``self`` whose call returns the logits. Outputs are written to
+``tests/golden/*.npz``. The fixtures travel with the repository; the reference does not.
 """
 
 from __future__ import annotations
 
+import __future__
 import argparse
+import ast
 import importlib.util
 import os
 import sys
@@ -166,6 +172,111 @@ def cases(ref):
     )
 
 
+def load_occupied_coordinates(reference_root: str):
+    """The reference's ``occupied_coordinates`` method, compiled alone from its source file."""
+
+    path = os.path.join(reference_root, "src", "mlx_diffuser", "models", "trellis.py")
+    with open(path) as f:
+        tree = ast.parse(f.read(), path)
+    for node in tree.body:
+        if isinstance(node, ast.ClassDef) and node.name == "TrellisSparseStructureDecoder":
+            for item in node.body:
+                if isinstance(item, ast.FunctionDef) and item.name == "occupied_coordinates":
+                    module = ast.Module(body=[item], type_ignores=[])
+                    code = compile(module, path, "exec",
+                                   flags=__future__.annotations.compiler_flag, dont_inherit=True)
+                    namespace = {"mx": sys.modules["mlx.core"], "np": np}
+                    exec(code, namespace)
+                    return namespace["occupied_coordinates"]
+    raise RuntimeError("occupied_coordinates not found in the reference")
+
+
+class _LogitsModel:
+    """Stand-in ``self`` for ``occupied_coordinates``: calling it returns the logits with a
+    trailing channel axis, like the decoder's (B, D, H, W, 1) output."""
+
+    def __init__(self, logits):
+        self.logits = logits
+
+    def __call__(self, _latent):
+        return self.logits[..., None]
+
+
+def topology_case(ref, reference_root: str) -> dict[str, np.ndarray]:
+    _, L = ref
+    mx = sys.modules["mlx.core"]
+    rng = np.random.default_rng(77)
+    out: dict[str, np.ndarray] = {}
+
+    # sparse_subdivide: negative coordinates, two batch elements, 2-D feature rows, and a scale
+    # that halves (4 -> 2) next to one that clamps (1 -> 1)
+    c = rng.integers(-5, 6, size=(37, 4)).astype(np.int32)
+    c[:, 0] = rng.integers(0, 2, size=37)
+    f = rng.standard_normal((37, 2, 3)).astype(np.float32)
+    t = L.SparseTensor(mx.array(f), mx.array(c), spatial_shape=(11, 12, 13), scale=(4, 1, 2))
+    sub = L.sparse_subdivide(t)
+    out["sub_coords_in"] = c
+    out["sub_features_in"] = f
+    out["sub_coords"] = np.asarray(sub.coords, np.int32)
+    out["sub_features"] = np.asarray(sub.features, np.float32)
+    out["sub_spatial_shape"] = np.asarray(sub.spatial_shape, np.int32)
+    out["sub_scale"] = np.asarray(sub.scale, np.int32)
+
+    # attention windows: three batch elements, negative coordinates, shifted windows
+    c = rng.integers(-9, 17, size=(300, 4)).astype(np.int32)
+    c[:, 0] = rng.integers(0, 3, size=300)
+    c = np.concatenate([c, c[:17]])  # duplicate rows land in one group
+    out["win_coords"] = c
+    t = L.SparseTensor(mx.zeros((len(c), 1)), mx.array(c))
+    cases = [(None, (0, 0, 0)), (8, (0, 0, 0)), (8, (4, 4, 4)), (3, (1, -2, 5))]
+    for i, (window, shift) in enumerate(cases):
+        groups = L._attention_groups(t, window, shift)
+        out[f"win{i}_window"] = np.int32(-1 if window is None else window)
+        out[f"win{i}_shift"] = np.asarray(shift, np.int32)
+        out[f"win{i}_perm"] = np.concatenate(groups).astype(np.int32)
+        out[f"win{i}_offsets"] = np.cumsum([0] + [len(g) for g in groups]).astype(np.int32)
+
+    # windowed self-attention and cross-attention through the reference's own code
+    heads, dim = 2, 8
+    q = rng.standard_normal((len(c), heads, dim)).astype(np.float32)
+    k = rng.standard_normal((len(c), heads, dim)).astype(np.float32)
+    v = rng.standard_normal((len(c), heads, dim)).astype(np.float32)
+    out["attn_q"], out["attn_k"], out["attn_v"] = q, k, v
+    for i, (window, shift) in enumerate(cases[1:3]):
+        o = L.sparse_self_attention(t, mx.array(q), mx.array(k), mx.array(v), window_size=window,
+                                    shift_window=shift)
+        out[f"attn{i}_out"] = np.asarray(o, np.float32)
+    order = np.argsort(c[:, 0], kind="stable")  # cross-attention wants batch-contiguous rows
+    cb = c[order]
+    tb = L.SparseTensor(mx.zeros((len(cb), 1)), mx.array(cb))
+    ctx_k = rng.standard_normal((3, 5, heads, dim)).astype(np.float32)
+    ctx_v = rng.standard_normal((3, 5, heads, dim)).astype(np.float32)
+    o = L.sparse_cross_attention(tb, mx.array(q), mx.array(ctx_k), mx.array(ctx_v))
+    out["cross_coords"] = cb
+    out["cross_k"], out["cross_v"] = ctx_k, ctx_v
+    out["cross_out"] = np.asarray(o, np.float32)
+
+    # occupancy -> coordinates, float32 and float16 logits, thresholds that need rounding
+    occupied = load_occupied_coordinates(reference_root)
+    logits = rng.standard_normal((2, 9, 10, 11)).astype(np.float32)
+    logits[0, 3, 4, 5] = np.nan
+    logits[1, 0, 0, 0] = np.float32(0.3)
+    out["occ_logits"] = logits
+    for i, thr in enumerate((0.0, 0.3, -1.25)):
+        out[f"occ{i}_threshold"] = np.float64(thr)
+        out[f"occ{i}_coords"] = np.asarray(occupied(_LogitsModel(mx.array(logits)), None, thr),
+                                           np.int32)
+    # float16(0.3) is above 0.3: a logit equal to it is above 0.3 but not above the rounded
+    # threshold the comparison uses
+    half = (rng.standard_normal((1, 7, 8, 9)) * 0.4).astype(np.float16)
+    half[0, 1, 2, 3] = np.float16(0.3)
+    out["occ_half_logits"] = half
+    out["occ_half_threshold"] = np.float64(0.3)
+    out["occ_half_coords"] = np.asarray(occupied(_LogitsModel(mx.array(half)), None, 0.3),
+                                        np.int32)
+    return out
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default=os.environ.get("MLX_DIFFUSER_REF", "/root/reference"))
@@ -175,6 +286,9 @@ def main() -> None:
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **data)
         print(f"{name}: N={len(data['coords'])} -> {os.path.relpath(path, ROOT)}")
+    path = os.path.join(HERE, "topology.npz")
+    np.savez_compressed(path, **topology_case(ref, args.reference))
+    print(f"topology -> {os.path.relpath(path, ROOT)}")
 
 
 if __name__ == "__main__":

@@ -81,6 +81,27 @@ def test_argument_errors_are_reported_before_any_launch():
     assert m.value == 0
     assert lib.sv_downsample_coords(None, 5, 0, None, None, None, None, ctypes.byref(m), None, 0,
                                     None) == N.SV_ERR_INVALID_ARGUMENT
+    # topology entry points: empty inputs succeed without touching the device, bad ones fail
+    shape = (ctypes.c_int64 * 4)(2, 0, 64, 64)
+    strides = (ctypes.c_int64 * 4)(0, 4096, 64, 1)
+    assert lib.sv_occupancy_workspace_bytes(shape) == 256
+    assert lib.sv_occupancy_workspace_bytes((ctypes.c_int64 * 4)(2, 64, 64, 64)) >= 2 * 512 * 4
+    assert lib.sv_occupancy_count(None, 0, shape, strides, 0.0, ctypes.byref(m), None, 0,
+                                  None) == N.SV_OK
+    assert m.value == 0
+    assert lib.sv_occupancy_count(None, 9, shape, strides, 0.0, ctypes.byref(m), None, 0,
+                                  None) == N.SV_ERR_BAD_DTYPE
+    neg = (ctypes.c_int64 * 4)(2, -1, 4, 4)
+    assert lib.sv_occupancy_count(None, 0, neg, strides, 0.0, ctypes.byref(m), None, 0,
+                                  None) == N.SV_ERR_INVALID_ARGUMENT
+    assert lib.sv_subdivide(None, 0, None, 0, None, None, None) == N.SV_OK
+    assert lib.sv_subdivide(None, -1, None, 0, None, None, None) == N.SV_ERR_INVALID_ARGUMENT
+    shift = (ctypes.c_int * 3)(0, 0, 0)
+    assert lib.sv_window_groups(None, 0, 8, shift, None, None, ctypes.byref(m), None, 0,
+                                None) == N.SV_OK
+    assert lib.sv_window_groups(None, 5, -2, shift, None, None, ctypes.byref(m), None, 0,
+                                None) == N.SV_ERR_INVALID_ARGUMENT
+    assert lib.sv_window_groups_workspace_bytes(100) > lib.sv_downsample_workspace_bytes(100)
     with pytest.raises(ValueError):
         N.check(N.SV_ERR_BAD_SHAPE, "x")
     with pytest.raises(RuntimeError):

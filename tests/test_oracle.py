@@ -102,3 +102,46 @@ def test_oracle_against_live_reference_random_cases():
             coords, inverse = O.downsample_coords(c, f)
             assert np.array_equal(coords, g[f"down{f}_coords"])
             assert np.array_equal(inverse, g[f"down{f}_inverse"])
+
+
+# ---- topology: subdivide, attention windows, occupancy -------------------------------------
+
+
+def _groups_as_perm(groups):
+    return np.concatenate(groups), np.cumsum([0] + [len(g) for g in groups])
+
+
+def test_subdivide_matches_reference(topology_golden):
+    g = topology_golden
+    coords, feats = O.subdivide(g["sub_coords_in"], g["sub_features_in"])
+    assert np.array_equal(coords, g["sub_coords"])
+    assert np.array_equal(feats, g["sub_features"])
+
+
+def test_attention_groups_match_reference(topology_golden):
+    g = topology_golden
+    i = 0
+    while f"win{i}_perm" in g:
+        window = int(g[f"win{i}_window"])
+        groups = O.attention_groups(g["win_coords"], None if window < 0 else window,
+                                    tuple(int(v) for v in g[f"win{i}_shift"]))
+        perm, offsets = _groups_as_perm(groups)
+        assert np.array_equal(perm, g[f"win{i}_perm"])
+        assert np.array_equal(offsets, g[f"win{i}_offsets"])
+        i += 1
+    assert i == 4
+
+
+def test_occupied_coordinates_match_reference(topology_golden):
+    g = topology_golden
+    for i in range(3):
+        got = O.occupied_coordinates(g["occ_logits"], float(g[f"occ{i}_threshold"]))
+        assert np.array_equal(got, g[f"occ{i}_coords"])
+    half = g["occ_half_logits"]
+    got = O.occupied_coordinates(half.astype(np.float32), float(g["occ_half_threshold"]),
+                                 "float16")
+    assert np.array_equal(got, g["occ_half_coords"])
+    # float16(0.3) > 0.3 and one logit equals it: a comparison against the unrounded
+    # threshold would list that cell
+    unrounded = np.argwhere(half.astype(np.float64) > float(g["occ_half_threshold"]))
+    assert len(unrounded) == len(g["occ_half_coords"]) + 1
