@@ -45,7 +45,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument(
         "--workload",
-        choices=["conv1024", "kmap", "pool", "scene128", "sweep", "halo", "topology"],
+        choices=["conv1024", "kmap", "pool", "scene128", "sweep", "halo", "topology", "resblock"],
         default="conv1024",
         help="conv1024 (default): the headline line above. The others run on one GPU and "
         "print one line each: kmap = kernel-map build on 16 x 128^3 at 8%% occupancy; pool = "
@@ -54,7 +54,9 @@ def parse_args():
         "{0.5, 2, 8, 30}%% x grid {64, 128}^3 x width {32, 128, 512, 1024}, batch 16; halo = "
         "the 128^3 scene Morton-partitioned over the torchrun ranks (strong scaling), convs "
         "64->64->32 each after an NCCL halo exchange; topology = occupancy -> coords on 16 x 64^3 "
-        "logits, sparse_subdivide and 8^3 attention windows of the 128^3 scene",
+        "logits, sparse_subdivide and 8^3 attention windows of the 128^3 scene; resblock = the SLat "
+        "I/O residual-block stack (128->128, 128->1024 down, 1024->128 up, 128->128) in fp16, "
+        "fused vs the reference's op-by-op sequence",
     )
     p.add_argument(
         "--profiling",
@@ -676,9 +678,126 @@ def run_workload(args) -> None:
                             "groups": groups},
                            _hbm_roofline(16.0 * n + 4.0 * n + 4.0 * (groups + 1), ms,
                                          "window grouping (key sort + first-row sort)")))
+    elif args.workload == "resblock":
+        lines.extend(resblock_lines(args, dev, flush))
     for line in lines:
         print(json.dumps(line), flush=True)
     N.check_device_status(dev)
+
+
+def resblock_lines(args, dev, flush) -> list:
+    """Four residual blocks of the SLat flow's I/O path on two 64^3 shells (fp16): fused
+    (SparseResBlock3D) and in the reference's op order (torch element-wise steps between the same
+    convolutions). Roofline time: per convolution max(F / tensor peak, B / HBM), plus one read
+    and one write of the rows for each row-norm pass."""
+
+    import torch
+    import torch.nn.functional as F
+
+    from mlx_diffuser_b200 import scenes
+    from mlx_diffuser_b200.layers.resblock import SparseResBlock3D
+    from mlx_diffuser_b200.layers.sparse import SparseTensor, sparse_downsample, sparse_upsample
+
+    dt = torch.float16
+    torch.manual_seed(0)
+    coords = scenes.batched([scenes.shell64(21), scenes.shell64(22)])
+    n = len(coords)
+    x = SparseTensor(torch.randn((n, 128), device=dev, dtype=dt), torch.from_numpy(coords).to(dev))
+    emb = torch.randn((2, 1024), device=dev, dtype=dt)
+    specs = [(128, 128, {}), (128, 1024, {"downsample": True}), (1024, 128, {"upsample": True}),
+             (128, 128, {})]
+    blocks = []
+    for cin, cout, kw in specs:
+        b = SparseResBlock3D(cin, 1024, out_channels=cout, **kw).to(dev)
+        w2 = torch.randn_like(b.conv2.conv.weight) / (27 * cout) ** 0.5
+        b.conv2.conv.weight = w2
+        b.cast_torso(dt)
+        blocks.append(b)
+
+    def fused():
+        h = x
+        for b in blocks:
+            h = b(h, emb)
+        return h
+
+    def ln32(h, w=None, bias=None):
+        return F.layer_norm(h.float(), (h.shape[-1],), w, bias, 1e-6).to(h.dtype)
+
+    def op_by_op():
+        h = x
+        for b in blocks:
+            lin = b.emb_layers[1]
+            scale, shift = torch.chunk(F.linear(F.silu(emb), lin.weight, lin.bias).to(dt), 2, -1)
+            if b.downsample:
+                h = sparse_downsample(h, 2)
+            elif b.upsample:
+                h = sparse_upsample(h, 2)
+            bi = h.coords[:, 0].long()
+            a = h.replace(F.silu(ln32(h.features, b.norm1.weight, b.norm1.bias)))
+            y = b.conv1(a)
+            y = y.replace(ln32(y.features) * (1 + scale[bi]) + shift[bi])
+            y = b.conv2(y.replace(F.silu(y.features)))
+            skip = b.skip_connection.project(h.features) if b.skip_connection is not None \
+                else h.features
+            h = y.replace(y.features + skip)
+        return h
+
+    from mlx_diffuser_b200.graphs import CapturedForward
+
+    def stack(feats, e):
+        h = SparseTensor(feats, x.coords, x.batch_size, x.spatial_shape, x.scale, x.cache)
+        for b in blocks:
+            h = b(h, e)
+        return h.features
+
+    out_f, out_r = fused(), op_by_op()
+    err = float((out_f.features.float() - out_r.features.float()).abs().max()
+                / out_r.features.float().abs().max())
+    graphed = CapturedForward(stack)
+    graph_exact = bool(torch.equal(graphed(x.features, emb), out_f.features))
+    ms_fused = _time_device(fused, args.steps, args.warmup, flush)
+    ms_ref = _time_device(op_by_op, args.steps, args.warmup, flush)
+    ms_graph = _time_device(lambda: graphed(x.features, emb), args.steps, args.warmup, flush)
+
+    peaks = measured_peaks()
+    roof_ms = 0.0
+    h = x
+    conv_flops = 0.0
+    for b, (cin, cout, kw) in zip(blocks, specs):
+        if kw.get("downsample"):
+            h = sparse_downsample(h, 2)
+        elif kw.get("upsample"):
+            h = sparse_upsample(h, 2)
+        m = h.num_points
+        nbr = h.cache.get("neighbors_3_1_" + str(h.scale))
+        pairs = int((nbr >= 0).sum().item()) if nbr is not None else 27 * m
+        for ci, co in ((cin, cout), (cout, cout)):
+            fl = 2.0 * ci * co * pairs
+            by = 2.0 * m * (ci + co) + 2.0 * 27 * ci * co + 4.0 * 27 * m
+            conv_flops += fl
+            roof_ms += max(fl / (peaks["bf16_tflops"] * 1e12), by / (peaks["hbm_gbs"] * 1e9)) * 1e3
+        roof_ms += (2.0 * m * cin * 2 + 2.0 * m * cout * 2) / (peaks["hbm_gbs"] * 1e9) * 1e3
+        h = b(h, emb)
+    base = {"workload": "slat_io_resblocks_shell64x2_fp16", "voxels": n,
+            "blocks": "128->128, 128->1024 down, 1024->128 up, 128->128",
+            "conv_flops": conv_flops, "roofline_ms": roof_ms,
+            "fused_vs_op_by_op_max_rel_diff": err}
+    base["graph_replay_bit_exact"] = graph_exact
+    graphed.release()
+    return [
+        _line("residual-block stack voxels/s", n / (ms_graph * 1e-3), "voxels/s", ms_graph, args,
+              dict(base, variant="fused, CUDA graph replay"),
+              {"bound": "tensor+hbm", "frac_of_roofline_time": roof_ms / ms_graph,
+               "peak_source": peaks["source"]}),
+        _line("residual-block stack voxels/s", n / (ms_fused * 1e-3), "voxels/s", ms_fused, args,
+              dict(base, variant="fused"),
+              {"bound": "tensor+hbm", "frac_of_roofline_time": roof_ms / ms_fused,
+               "peak_source": peaks["source"]}),
+        _line("residual-block stack voxels/s", n / (ms_ref * 1e-3), "voxels/s", ms_ref, args,
+              dict(base, variant="reference op order (torch element-wise)"),
+              {"bound": "tensor+hbm", "frac_of_roofline_time": roof_ms / ms_ref,
+               "peak_source": peaks["source"]}),
+    ]
 
 
 def run_halo(args) -> None:

@@ -18,6 +18,7 @@
  *   src/mlx_diffuser/layers/sparse.py:298-318   sparse_subdivide
  *   src/mlx_diffuser/layers/sparse.py:321-342   _attention_groups (sparse_self_attention)
  *   src/mlx_diffuser/models/trellis.py:278-285  occupied_coordinates (np.argwhere step)
+ *   src/mlx_diffuser/models/trellis_slat.py:71-82 _SparseResBlock3D norms, modulation, skip add
  */
 #ifndef SPARSEVOX_H_
 #define SPARSEVOX_H_
@@ -138,6 +139,19 @@ SV_API int sv_conv3d_forward(const void* features, int64_t n, int cin, const int
                              void* workspace, size_t workspace_bytes, int32_t* status,
                              sv_stream_t stream);
 
+/* sv_conv3d_forward plus a residual: out = conv + bias + residual, summed in fp32 and rounded
+ * once. residual [n, cout] in `dtype` (nullable = none; 16-byte aligned for the tensor-core
+ * path) may be the same buffer as `out` (an in-place add), but must not partially overlap it.
+ * It is the `h + skip` of the reference's sparse residual block
+ * (src/mlx_diffuser/models/trellis_slat.py:82), folded into the convolution's epilogue. */
+SV_API int sv_conv3d_forward_residual(const void* features, int64_t n, int cin,
+                                      const int32_t* nbr, int kvol, const int32_t* row_order,
+                                      const int32_t* tile_order, const void* weight, int layout,
+                                      const void* bias, const void* residual, int cout, int dtype,
+                                      void* out, int algo, void* workspace,
+                                      size_t workspace_bytes, int32_t* status,
+                                      sv_stream_t stream);
+
 /* Repack a (K, Cin, Cout) weight into spconv's (Cout, K, Cin) layout. */
 SV_API int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int cout, int dtype,
                                 void* w_oki, sv_stream_t stream);
@@ -169,6 +183,21 @@ SV_API int sv_downsample_features(const void* features, int64_t n, int channels,
 SV_API int sv_upsample_features(const void* coarse, int64_t m, int channels, int dtype,
                                 const int32_t* inverse, int64_t n, void* out, int32_t* status,
                                 sv_stream_t stream);
+
+/* ---- residual-block row normalisation ------------------------------------------------- */
+
+/* out[r] = act(mod(LayerNorm32(x[r]))) per row r of x [n, channels] (even, <= 4096):
+ *   LayerNorm32: (x - mean) * rsqrt(mean((x - mean)^2) + eps), fp32, then * weight + bias when
+ *     weight [channels] (fp32) is given (src/mlx_diffuser/layers/trellis.py:16-43);
+ *   mod: * (1 + scale[b]) + shift[b] when scale / shift [batch, channels] (in `dtype`) are
+ *     given, b = coords[r, 0] (the modulation of src/mlx_diffuser/models/trellis_slat.py:79);
+ *   act: silu when `silu` is nonzero.
+ * Computed in fp32 and rounded once to `dtype`; out may be x (in place). A batch index outside
+ * [0, batch) ORs SV_DEVICE_BAD_INDEX into `status` and that row is not modulated. */
+SV_API int sv_rownorm(const void* x, int64_t n, int channels, int dtype, float eps,
+                      const float* weight, const float* bias, const void* scale,
+                      const void* shift, const int32_t* coords, int64_t batch, int silu,
+                      void* out, int32_t* status, sv_stream_t stream);
 
 /* ---- topology: occupancy -> coordinates, subdivision, attention windows --------------- */
 

@@ -59,7 +59,16 @@ _SIGNATURES = {
         _I32,
         [_P, _I64, _I32, _P, _I32, _P, _P, _P, _I32, _P, _I32, _I32, _P, _I32, _P, _SZ, _P, _P],
     ),
+    "sv_conv3d_forward_residual": (
+        _I32,
+        [_P, _I64, _I32, _P, _I32, _P, _P, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _P, _SZ, _P,
+         _P],
+    ),
     "sv_weight_kio_to_oki": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P]),
+    "sv_rownorm": (
+        _I32,
+        [_P, _I64, _I32, _I32, ctypes.c_float, _P, _P, _P, _P, _P, _I64, _I32, _P, _P, _P],
+    ),
     "sv_downsample_workspace_bytes": (_SZ, [_I64]),
     "sv_downsample_coords": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "sv_downsample_features": (_I32, [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P]),

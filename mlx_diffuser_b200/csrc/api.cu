@@ -96,6 +96,18 @@ extern "C" int sv_conv3d_forward(const void* features, int64_t n, int cin, const
                                  int layout, const void* bias, int cout, int dtype, void* out,
                                  int algo, void* workspace, size_t workspace_bytes,
                                  int32_t* status, sv_stream_t stream) {
+  return sv_conv3d_forward_residual(features, n, cin, nbr, kvol, row_order, tile_order, weight,
+                                    layout, bias, nullptr, cout, dtype, out, algo, workspace,
+                                    workspace_bytes, status, stream);
+}
+
+extern "C" int sv_conv3d_forward_residual(const void* features, int64_t n, int cin,
+                                          const int32_t* nbr, int kvol,
+                                          const int32_t* row_order, const int32_t* tile_order,
+                                          const void* weight, int layout, const void* bias,
+                                          const void* residual, int cout, int dtype, void* out,
+                                          int algo, void* workspace, size_t workspace_bytes,
+                                          int32_t* status, sv_stream_t stream) {
   if (n < 0 || cin < 0 || cout < 0 || kvol < 1)
     SV_FAIL(SV_ERR_BAD_SHAPE, "sv_conv3d_forward: negative size or empty kernel");
   if (!valid_dtype(dtype)) SV_FAIL(SV_ERR_BAD_DTYPE, "sv_conv3d_forward: unknown dtype");
@@ -108,12 +120,12 @@ extern "C" int sv_conv3d_forward(const void* features, int64_t n, int cin, const
     SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward: null pointer");
   cudaStream_t s = to_stream(stream);
   ConvArgs a{features, n, cin, nbr, kvol, row_order, weight, layout, bias, cout, dtype, out,
-             status};
+             status, residual};
   const bool use_tc = tc_path(a, algo) && aligned16(weight);
   if (algo == SV_CONV_TCGEN05 && !use_tc)
     SV_FAIL(SV_ERR_UNSUPPORTED,
             "tcgen05 convolution needs fp16/bf16, Cin % 32 == 0, Cout % 32 == 0, kernel volume "
-            "<= 27 and 16-byte aligned features/weight/out");
+            "<= 27 and 16-byte aligned features/weight/out/residual");
   if (!use_tc) return conv_simt_launch(a, s);
   const size_t need = sv_conv3d_workspace_bytes(n, cin, cout, kvol, dtype, layout, algo);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))

@@ -19,6 +19,7 @@ struct ConvArgs {
   int dtype;                 // sv_dtype of features / weight / bias / out
   void* out;                 // [n, cout]
   int32_t* status;           // device status word or null
+  const void* residual;      // [n, cout] added before rounding, or null; may equal `out`
 };
 
 // CUDA-core kernel: any dtype, shape and layout.

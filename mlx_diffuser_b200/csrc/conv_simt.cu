@@ -21,7 +21,7 @@ template <typename T, int LAYOUT>
 __global__ void __launch_bounds__(256) conv_simt_kernel(
     const T* __restrict__ feat, int64_t n, int cin, const int32_t* __restrict__ nbr, int kvol,
     const int32_t* __restrict__ row_order, const T* __restrict__ w, const T* __restrict__ bias,
-    int cout, T* __restrict__ out, int32_t* status) {
+    const T* residual, int cout, T* out, int32_t* status) {
   __shared__ __align__(16) float As[SBK][SBM];
   __shared__ __align__(16) float Bs[SBK][SBN];
   __shared__ int32_t s_src[SBM];
@@ -114,7 +114,8 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(
       const int co = col0 + tx * 4 + j;
       if (co < cout) {
         const float b = bias ? to_f32(bias[co]) : 0.f;
-        out[(int64_t)o * cout + co] = from_f32<T>(acc[i][j] + b);
+        const float r = residual ? to_f32(residual[(int64_t)o * cout + co]) : 0.f;
+        out[(int64_t)o * cout + co] = from_f32<T>(acc[i][j] + b + r);
       }
     }
   }
@@ -126,14 +127,15 @@ int launch_typed(const ConvArgs& a, cudaStream_t s) {
   const T* f = static_cast<const T*>(a.features);
   const T* w = static_cast<const T*>(a.weight);
   const T* b = static_cast<const T*>(a.bias);
+  const T* r = static_cast<const T*>(a.residual);
   T* o = static_cast<T*>(a.out);
   if (a.layout == SV_WEIGHT_KIO)
     conv_simt_kernel<T, SV_WEIGHT_KIO><<<grid, 256, 0, s>>>(f, a.n, a.cin, a.nbr, a.kvol,
-                                                            a.row_order, w, b, a.cout, o,
+                                                            a.row_order, w, b, r, a.cout, o,
                                                             a.status);
   else
     conv_simt_kernel<T, SV_WEIGHT_OKI><<<grid, 256, 0, s>>>(f, a.n, a.cin, a.nbr, a.kvol,
-                                                            a.row_order, w, b, a.cout, o,
+                                                            a.row_order, w, b, r, a.cout, o,
                                                             a.status);
   SV_LAUNCH_CHECK();
   return SV_OK;

@@ -23,9 +23,9 @@
 //               cp.async -- whole rows per group of threads, so a warp instruction reads
 //               complete rows -- zero-filled for missing neighbours, in the swizzled layout TMA
 //               would write;
-//   warps 6-9   epilogue: tcgen05.ld of 32 accumulator columns at a time, + bias, round,
-//               16-byte stores to the row's output; it drains one accumulator while the MMA
-//               fills the other;
+//   warps 6-9   epilogue: tcgen05.ld of 32 accumulator columns at a time, + bias (+ the
+//               residual row, when given), round, 16-byte stores to the row's output; it drains
+//               one accumulator while the MMA fills the other;
 //   warps 10-13 stagers: fetch the next work item and stage its rows and their neighbour
 //               lists (one row per thread, double-buffered) while the current item runs.
 // Barriers: a stage ring (full/empty; 4 to 8 deep depending on BN), two accumulator buffers
@@ -126,12 +126,12 @@ __device__ __forceinline__ void decode_item(const Sched& sc, int32_t item, int32
   *n0 = nt * BN;
 }
 
-template <int BN, int BK, typename T>
+template <int BN, int BK, typename T, bool kResidual>
 __global__ void __launch_bounds__(TTHREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T* __restrict__ feat,
                    int n, int cin, const int32_t* __restrict__ nbr, int kvol,
-                   const int32_t* __restrict__ row_order, const T* __restrict__ bias, int cout,
-                   T* __restrict__ out, Sched sc, int32_t* status) {
+                   const int32_t* __restrict__ row_order, const T* __restrict__ bias,
+                   const T* residual, int cout, T* out, Sched sc, int32_t* status) {
   using L = TcLayout<BN, BK>;
   constexpr int S = L::STAGES;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -344,6 +344,18 @@ __global__ void __launch_bounds__(TTHREADS, 1)
         }
         if (orow >= 0) {
           const int c0 = w.n0 + ch * 32;
+          uint32_t res[16];
+          if constexpr (kResidual) {
+            const uint4* src = reinterpret_cast<const uint4*>(residual + (int64_t)orow * cout + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 r4 = src[j];
+              res[4 * j] = r4.x;
+              res[4 * j + 1] = r4.y;
+              res[4 * j + 2] = r4.z;
+              res[4 * j + 3] = r4.w;
+            }
+          }
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -352,6 +364,11 @@ __global__ void __launch_bounds__(TTHREADS, 1)
             if (bias) {
               lo += to_f32(bias[c0 + 2 * j]);
               hi += to_f32(bias[c0 + 2 * j + 1]);
+            }
+            if constexpr (kResidual) {
+              const T* r2 = reinterpret_cast<const T*>(&res[j]);
+              lo += to_f32(r2[0]);
+              hi += to_f32(r2[1]);
             }
             packed[j] = pack2<T>(lo, hi);
           }
@@ -477,7 +494,7 @@ int weight_map(const ConvArgs& a, bool bf16, int box_k, int box_rows, CUtensorMa
   return SV_OK;
 }
 
-template <int BN, int BK, typename T>
+template <int BN, int BK, typename T, bool kResidual>
 int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
   using L = TcLayout<BN, BK>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -485,7 +502,7 @@ int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cu
   SV_CUDA_TRY(cudaGetDevice(&dev));
   static bool attr_done[256] = {};
   if (dev >= 256 || !attr_done[dev]) {
-    SV_CUDA_TRY(cudaFuncSetAttribute(conv_tc_kernel<BN, BK, T>,
+    SV_CUDA_TRY(cudaFuncSetAttribute(conv_tc_kernel<BN, BK, T, kResidual>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
     if (dev < 256) attr_done[dev] = true;
   }
@@ -503,26 +520,34 @@ int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cu
   const int grid = (int)std::min<int64_t>(items, num_sms());
   sc.total_items = (int32_t)items;
   SV_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int32_t), s));
-  conv_tc_kernel<BN, BK, T><<<grid, TTHREADS, L::SMEM, s>>>(
+  conv_tc_kernel<BN, BK, T, kResidual><<<grid, TTHREADS, L::SMEM, s>>>(
       tmap, static_cast<const T*>(a.features), (int)a.n, a.cin, a.nbr, a.kvol,
-      a.row_order, static_cast<const T*>(a.bias), a.cout, static_cast<T*>(a.out), sc, a.status);
+      a.row_order, static_cast<const T*>(a.bias), static_cast<const T*>(a.residual), a.cout,
+      static_cast<T*>(a.out), sc, a.status);
   SV_LAUNCH_CHECK();
   return SV_OK;
 }
 
-template <int BK, typename T>
+template <int BK, typename T, bool kResidual>
 int launch_bk(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
-  if (a.cout % 256 == 0) return launch_bn<256, BK, T>(a, tile_order, counter, s);
-  if (a.cout % 128 == 0) return launch_bn<128, BK, T>(a, tile_order, counter, s);
-  if (a.cout % 64 == 0) return launch_bn<64, BK, T>(a, tile_order, counter, s);
-  return launch_bn<32, BK, T>(a, tile_order, counter, s);
+  if (a.cout % 256 == 0) return launch_bn<256, BK, T, kResidual>(a, tile_order, counter, s);
+  if (a.cout % 128 == 0) return launch_bn<128, BK, T, kResidual>(a, tile_order, counter, s);
+  if (a.cout % 64 == 0) return launch_bn<64, BK, T, kResidual>(a, tile_order, counter, s);
+  return launch_bn<32, BK, T, kResidual>(a, tile_order, counter, s);
+}
+
+template <typename T, bool kResidual>
+int launch_res(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
+               cudaStream_t s) {
+  if (a.cin % 64 == 0) return launch_bk<64, T, kResidual>(a, tile_order, counter, s);
+  return launch_bk<32, T, kResidual>(a, tile_order, counter, s);
 }
 
 template <typename T>
 int launch_typed(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
                  cudaStream_t s) {
-  if (a.cin % 64 == 0) return launch_bk<64, T>(a, tile_order, counter, s);
-  return launch_bk<32, T>(a, tile_order, counter, s);
+  if (a.residual) return launch_res<T, true>(a, tile_order, counter, s);
+  return launch_res<T, false>(a, tile_order, counter, s);
 }
 
 }  // namespace
@@ -531,7 +556,8 @@ bool conv_tc_supported(const ConvArgs& a) {
   return (a.dtype == SV_FLOAT16 || a.dtype == SV_BFLOAT16) && a.layout == SV_WEIGHT_OKI &&
          a.cin > 0 && a.cin % 32 == 0 && a.cout > 0 && a.cout % 32 == 0 && a.kvol >= 1 &&
          a.kvol <= TMAX_KVOL && a.n <= INT32_MAX - TBM && (int64_t)a.kvol * a.cin < INT32_MAX &&
-         aligned16(a.features) && aligned16(a.weight) && aligned16(a.out);
+         aligned16(a.features) && aligned16(a.weight) && aligned16(a.out) &&
+         aligned16(a.residual);
 }
 
 int conv_tc_launch(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,

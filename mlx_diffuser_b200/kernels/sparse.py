@@ -42,10 +42,12 @@ def conv3d_forward(
     tile_order: torch.Tensor | None = None,
     algo: int = N.SV_CONV_AUTO,
     out: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Call ``sv_conv3d_forward``. Tensors must already be contiguous, on one CUDA device, and
-    share the feature dtype (``neighbors`` int32); ``layout`` is SV_WEIGHT_KIO or _OKI.
-    ``row_order`` / ``tile_order`` are the schedule from :func:`conv_row_order`."""
+    """Call ``sv_conv3d_forward_residual``. Tensors must already be contiguous, on one CUDA
+    device, and share the feature dtype (``neighbors`` int32); ``layout`` is SV_WEIGHT_KIO or
+    _OKI. ``row_order`` / ``tile_order`` are the schedule from :func:`conv_row_order`.
+    ``residual`` ([n, cout], optional, may be ``out``) is added to the result before rounding."""
 
     n, cin = features.shape
     kvol = neighbors.shape[1]
@@ -58,7 +60,11 @@ def conv3d_forward(
     lib = N.load()
     ws_bytes = lib.sv_conv3d_workspace_bytes(n, cin, cout, kvol, dcode, layout, algo)
     ws = N.workspace(ws_bytes, dev) if ws_bytes else None
-    rc = lib.sv_conv3d_forward(
+    if residual is not None and (tuple(residual.shape) != (n, cout)
+                                 or residual.dtype != features.dtype
+                                 or not residual.is_contiguous()):
+        raise ValueError(f"residual must be a contiguous ({n}, {cout}) {features.dtype} tensor")
+    rc = lib.sv_conv3d_forward_residual(
         features.data_ptr(),
         n,
         cin,
@@ -69,6 +75,7 @@ def conv3d_forward(
         weight.data_ptr(),
         layout,
         N.ptr(bias),
+        N.ptr(residual),
         cout,
         dcode,
         out.data_ptr(),

@@ -303,7 +303,10 @@ class SparseConv3D(nn.Module):
             )
         return self._operand_cache[1], self._operand_cache[2]
 
-    def forward(self, x: SparseTensor) -> SparseTensor:
+    def forward(self, x: SparseTensor, residual: torch.Tensor | None = None) -> SparseTensor:
+        """``residual`` (optional, ``[N, Cout]`` in the feature dtype) is added to the output in
+        the convolution's epilogue: ``conv(x) + residual`` with one rounding."""
+
         key = f"neighbors_{self.kernel_size}_{self.dilation}_{x.scale}"
         neighbors = x.cache.get(key)
         if neighbors is None:
@@ -328,6 +331,7 @@ class SparseConv3D(nn.Module):
         out = conv3d_forward(
             features.contiguous(), neighbors, weight, N.SV_WEIGHT_OKI, bias, o,
             row_order=row_order, tile_order=tile_order, algo=self.algo,
+            residual=None if residual is None else residual.contiguous(),
         )
         return x.replace(out)
 
@@ -346,25 +350,37 @@ def sparse_downsample(x: SparseTensor, factor: int = 2) -> SparseTensor:
 
     if factor < 1:
         raise ValueError("factor must be positive")
-    coords = x.coords.contiguous()
-    N.require_cuda(coords, "coords")
-    dev = coords.device
-    n = coords.shape[0]
+    N.require_cuda(x.coords, "coords")
+    dev = x.coords.device
+    n = x.coords.shape[0]
     lib = N.load()
-    new_coords = torch.empty((n, 4), dtype=torch.int32, device=dev)
-    inverse = torch.empty(n, dtype=torch.int32, device=dev)
-    sorted_rows = torch.empty(n, dtype=torch.int32, device=dev)
-    seg = torch.empty(n + 1, dtype=torch.int32, device=dev)
-    m_out = ctypes.c_int64(0)
-    ws_bytes = lib.sv_downsample_workspace_bytes(n)
-    ws = N.workspace(ws_bytes, dev)
-    rc = lib.sv_downsample_coords(
-        coords.data_ptr(), n, factor, new_coords.data_ptr(), inverse.data_ptr(),
-        sorted_rows.data_ptr(), seg.data_ptr(), ctypes.byref(m_out), ws.data_ptr(), ws_bytes,
-        N.stream(dev),
-    )
-    N.check(rc, "sparse_downsample")
-    m = int(m_out.value)
+    # The coarse coordinates depend only on the fine ones. They are kept in the shared cache
+    # with the coords tensor they came from (held, so its memory cannot be reused) and its
+    # version counter, so a repeated downsample of the same topology -- every step of a
+    # sampler -- skips the sort and its host synchronisation.
+    coords_key = f"downsample_coords_{factor}_{x.scale}"
+    hit = x.cache.get(coords_key)
+    if hit is not None and hit[0] is x.coords and hit[1] == x.coords._version:
+        _, _, new_coords, inverse, sorted_rows, seg, m = hit
+    else:
+        coords = x.coords.contiguous()
+        new_coords = torch.empty((n, 4), dtype=torch.int32, device=dev)
+        inverse = torch.empty(n, dtype=torch.int32, device=dev)
+        sorted_rows = torch.empty(n, dtype=torch.int32, device=dev)
+        seg = torch.empty(n + 1, dtype=torch.int32, device=dev)
+        m_out = ctypes.c_int64(0)
+        ws_bytes = lib.sv_downsample_workspace_bytes(n)
+        ws = N.workspace(ws_bytes, dev)
+        rc = lib.sv_downsample_coords(
+            coords.data_ptr(), n, factor, new_coords.data_ptr(), inverse.data_ptr(),
+            sorted_rows.data_ptr(), seg.data_ptr(), ctypes.byref(m_out), ws.data_ptr(),
+            ws_bytes, N.stream(dev),
+        )
+        N.check(rc, "sparse_downsample")
+        m = int(m_out.value)
+        new_coords = new_coords[:m]
+        x.cache[coords_key] = (x.coords, x.coords._version, new_coords, inverse, sorted_rows,
+                               seg, m)
     feats = x.features
     trailing = feats.shape[1:]
     flat = feats.reshape(n, math.prod(trailing)).contiguous()
@@ -385,7 +401,7 @@ def sparse_downsample(x: SparseTensor, factor: int = 2) -> SparseTensor:
         math.ceil(source_shape[1] / factor),
         math.ceil(source_shape[2] / factor),
     )
-    out = SparseTensor(features, new_coords[:m], x.batch_size, spatial_shape, scale, x.cache)
+    out = SparseTensor(features, new_coords, x.batch_size, spatial_shape, scale, x.cache)
     out.cache[f"upsample_{factor}_{scale}"] = (x.coords, inverse, x.spatial_shape, x.scale)
     return out
 

@@ -18,7 +18,8 @@ Covered surface (each item is what those two reference files call):
   fallback (``use_metal=False``) can run;
 * ``fast.scaled_dot_product_attention`` -- a float64 softmax attention, for the reference's
   ``sparse_self_attention`` / ``sparse_cross_attention``;
-* ``arange``;
+* ``arange / split / mean / square / rsqrt``;
+* ``nn.Linear``, ``nn.SiLU`` and ``nn.silu``, for the residual block around the convolutions;
 * ``nn.Module`` with ``training`` / ``eval()`` / ``train()``.
 """
 
@@ -121,6 +122,23 @@ def allclose(a, b, rtol=1e-5, atol=1e-8):
     return bool(np.allclose(np.asarray(a), np.asarray(b), rtol=rtol, atol=atol))
 
 
+def split(a, sections, axis=0):
+    return [_wrap(p) for p in np.split(np.asarray(a), sections, axis=axis)]
+
+
+def mean(a, axis=None, keepdims=False):
+    return _wrap(np.mean(np.asarray(a), axis=axis, keepdims=keepdims))
+
+
+def square(a):
+    return _wrap(np.square(np.asarray(a)))
+
+
+def rsqrt(a):
+    a = np.asarray(a)
+    return _wrap((1.0 / np.sqrt(a)).astype(a.dtype))
+
+
 def arange(start, stop=None, step=1, dtype=None):
     return _wrap(np.arange(start, stop, step, dtype=dtype))
 
@@ -176,6 +194,11 @@ class _Fast(types.ModuleType):
 fast = _Fast()
 
 
+def _silu(x):
+    x = np.asarray(x)
+    return _wrap((x / (1.0 + np.exp(-x))).astype(x.dtype))
+
+
 class Module:
     """Minimal ``mlx.nn.Module``: attribute container with a training flag."""
 
@@ -191,12 +214,37 @@ class Module:
         return self
 
 
+class SiLU(Module):
+    def __call__(self, x):
+        return _silu(x)
+
+
+class Linear(Module):
+    """``mlx.nn.Linear``: weight (out, in) uniform in ±1/sqrt(in), bias zeros."""
+
+    def __init__(self, input_dims: int, output_dims: int, bias: bool = True):
+        super().__init__()
+        bound = 1.0 / np.sqrt(input_dims)
+        self.weight = random.uniform(-bound, bound, (output_dims, input_dims))
+        if bias:
+            self.bias = zeros((output_dims,))
+
+    def __call__(self, x):
+        y = np.asarray(x) @ np.asarray(self.weight).T
+        if hasattr(self, "bias"):
+            y = y + np.asarray(self.bias)
+        return _wrap(y)
+
+
 def install() -> None:
     """Register this shim as ``mlx`` / ``mlx.core`` / ``mlx.nn`` in ``sys.modules``."""
 
     core = sys.modules[__name__]
     nn = types.ModuleType("mlx.nn")
     nn.Module = Module
+    nn.Linear = Linear
+    nn.SiLU = SiLU
+    nn.silu = _silu
     pkg = types.ModuleType("mlx")
     pkg.__path__ = []
     pkg.core = core

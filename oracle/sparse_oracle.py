@@ -310,3 +310,47 @@ def round_to_bf16(values) -> np.ndarray:
     rounded = (bits + 0x7FFF + ((bits >> 16) & 1)) & 0xFFFF0000
     out = rounded.astype(np.uint32).view(np.float32)
     return np.where(np.isnan(v), v, out)
+
+
+# --------------------------------------------------------------------------------------------
+# residual block around the convolutions
+# --------------------------------------------------------------------------------------------
+
+
+def layernorm32(h, weight=None, bias=None, eps: float = 1e-6) -> np.ndarray:
+    """``LayerNorm32`` (``src/mlx_diffuser/layers/trellis.py:16-43``) in float32."""
+
+    h = np.asarray(h, np.float32)
+    mean = h.mean(-1, keepdims=True)
+    var = np.square(h - mean).mean(-1, keepdims=True)
+    h = (h - mean) / np.sqrt(var + np.float32(eps))
+    if weight is not None:
+        h = h * weight + bias
+    return h.astype(np.float32)
+
+
+def silu(h) -> np.ndarray:
+    h = np.asarray(h, np.float32)
+    return (h / (1.0 + np.exp(-h))).astype(np.float32)
+
+
+def resblock(coords, feats, emb, p: dict, *, nbr=None) -> np.ndarray:
+    """``_SparseResBlock3D.__call__`` after its optional resampling
+    (``src/mlx_diffuser/models/trellis_slat.py:71-82``), float32: ``p`` holds norm1_w/_b,
+    conv1_w/_b, conv2_w/_b (spconv layout), emb_w/_b and optionally skip_w/_b. The modulation
+    rows are picked by the batch column when ``emb`` has one row per batch element."""
+
+    coords = np.asarray(coords, np.int32)
+    if nbr is None:
+        nbr = build_neighbor_map(coords, 3)
+    proj = silu(emb) @ p["emb_w"].T + p["emb_b"]
+    scale, shift = np.split(proj.astype(np.float32), 2, axis=-1)
+    batch_size = int(coords[:, 0].max()) + 1 if len(coords) else 0
+    if scale.shape[0] == batch_size:
+        scale, shift = scale[coords[:, 0]], shift[coords[:, 0]]
+    a = silu(layernorm32(feats, p["norm1_w"], p["norm1_b"]))
+    h = sparse_conv3d(a, nbr, spconv_weight_to_kio(p["conv1_w"]), p["conv1_b"])
+    h = layernorm32(h) * (1 + scale) + shift
+    h = sparse_conv3d(silu(h), nbr, spconv_weight_to_kio(p["conv2_w"]), p["conv2_b"])
+    skip = feats @ p["skip_w"].T + p["skip_b"] if "skip_w" in p else feats
+    return (h + skip).astype(np.float32)

@@ -21,6 +21,7 @@ def pytest_configure(config):
 
 
 TOPOLOGY = "topology"  # subdivide / attention windows / occupancy fixture, not a conv case
+RESBLOCK = "resblock"  # residual-block fixture
 
 
 def golden_names() -> list[str]:
@@ -28,7 +29,7 @@ def golden_names() -> list[str]:
 
     names = (os.path.splitext(os.path.basename(p))[0]
              for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
-    return sorted(n for n in names if n != TOPOLOGY)
+    return sorted(n for n in names if n not in (TOPOLOGY, RESBLOCK))
 
 
 def load_golden(name: str) -> dict[str, np.ndarray]:
@@ -44,3 +45,8 @@ def golden(request):
 @pytest.fixture(scope="session")
 def topology_golden():
     return load_golden(TOPOLOGY)
+
+
+@pytest.fixture(scope="session")
+def resblock_golden():
+    return load_golden(RESBLOCK)

@@ -8,7 +8,9 @@ MLX cannot be installed here, so the reference files ``src/mlx_diffuser/kernels/
 and ``src/mlx_diffuser/layers/sparse.py`` are executed unmodified on top of the NumPy stand-in
 ``oracle/mlx_shim.py``: ``build_neighbor_map``, ``SparseConv3D`` (its pure fallback,
 ``use_metal=False``), ``sparse_downsample``, ``sparse_upsample``, ``sparse_subdivide``,
-``_attention_groups``, ``sparse_self_attention`` and ``sparse_cross_attention``. The
+``_attention_groups``, ``sparse_self_attention`` and ``sparse_cross_attention``; the
+residual block ``_SparseResBlock3D`` (``src/mlx_diffuser/models/trellis_slat.py:43-92``) with
+``LayerNorm32`` and ``SparseLinear`` is compiled from its files by ``ast``, as written. The
 occupancy step ``TrellisSparseStructureDecoder.occupied_coordinates``
 (``src/mlx_diffuser/models/trellis.py:278-285``) is taken out of its file by ``ast`` and run as
 written, with a stand-in ``self`` whose call returns the logits. Outputs are written to
@@ -202,6 +204,82 @@ class _LogitsModel:
         return self.logits[..., None]
 
 
+def load_classes(reference_root: str, relpath: str, names: tuple[str, ...], namespace: dict):
+    """Compile the named classes of one reference file, as written, into ``namespace``."""
+
+    path = os.path.join(reference_root, "src", "mlx_diffuser", relpath)
+    with open(path) as f:
+        tree = ast.parse(f.read(), path)
+    body = [n for n in tree.body if isinstance(n, ast.ClassDef) and n.name in names]
+    if len(body) != len(names):
+        raise RuntimeError(f"{names} not all found in {relpath}")
+    code = compile(ast.Module(body=body, type_ignores=[]), path, "exec",
+                   flags=__future__.annotations.compiler_flag, dont_inherit=True)
+    exec(code, namespace)
+
+
+def resblock_case(ref, reference_root: str) -> dict[str, np.ndarray]:
+    """The reference's _SparseResBlock3D (with its LayerNorm32 and SparseLinear) in float32 on
+    seeded parameters: a plain block with a linear skip, a downsampling block and an upsampling
+    block fed by the downsampling block's output."""
+
+    _, L = ref
+    mx = sys.modules["mlx.core"]
+    ns = {"mx": mx, "nn": sys.modules["mlx.nn"], "math": __import__("math"), "np": np,
+          "SparseTensor": L.SparseTensor, "SparseConv3D": L.SparseConv3D,
+          "sparse_downsample": L.sparse_downsample, "sparse_upsample": L.sparse_upsample}
+    load_classes(reference_root, "layers/trellis.py", ("LayerNorm32",), ns)
+    load_classes(reference_root, "layers/trellis_sparse.py", ("SparseLinear",), ns)
+    load_classes(reference_root, "models/trellis_slat.py", ("_SparseResBlock3D",), ns)
+    block_cls = ns["_SparseResBlock3D"]
+    rng = np.random.default_rng(99)
+    out: dict[str, np.ndarray] = {}
+
+    def build(prefix, cin, cout, emb_ch, **kw):
+        blk = block_cls(cin, emb_ch, out_channels=cout, use_metal=False, **kw)
+        p = {
+            "norm1_w": (1 + 0.1 * rng.standard_normal(cin)).astype(np.float32),
+            "norm1_b": (0.1 * rng.standard_normal(cin)).astype(np.float32),
+            "conv1_w": scenes.conv_weight(cout, cin, 3, int(rng.integers(1 << 30))),
+            "conv1_b": (0.1 * rng.standard_normal(cout)).astype(np.float32),
+            "conv2_w": scenes.conv_weight(cout, cout, 3, int(rng.integers(1 << 30))),
+            "conv2_b": (0.1 * rng.standard_normal(cout)).astype(np.float32),
+            "emb_w": (rng.standard_normal((2 * cout, emb_ch)) / np.sqrt(emb_ch)).astype(np.float32),
+            "emb_b": (0.1 * rng.standard_normal(2 * cout)).astype(np.float32),
+        }
+        blk.norm1.weight, blk.norm1.bias = mx.array(p["norm1_w"]), mx.array(p["norm1_b"])
+        blk.conv1.conv.weight, blk.conv1.conv.bias = mx.array(p["conv1_w"]), mx.array(p["conv1_b"])
+        blk.conv2.conv.weight, blk.conv2.conv.bias = mx.array(p["conv2_w"]), mx.array(p["conv2_b"])
+        blk.emb_layers[1].weight = mx.array(p["emb_w"])
+        blk.emb_layers[1].bias = mx.array(p["emb_b"])
+        if blk.skip_connection is not None:
+            p["skip_w"] = (rng.standard_normal((cout, cin)) / np.sqrt(cin)).astype(np.float32)
+            p["skip_b"] = (0.1 * rng.standard_normal(cout)).astype(np.float32)
+            blk.skip_connection.weight = mx.array(p["skip_w"])
+            blk.skip_connection.bias = mx.array(p["skip_b"])
+        for k, v in p.items():
+            out[f"{prefix}_{k}"] = v
+        return blk
+
+    coords = scenes.batched([scenes.shell(16, 5.5, 2.0, 1.0, seed=51),
+                             scenes.shell(16, 6.5, 2.0, 1.0, seed=52)])
+    feats = rng.standard_normal((len(coords), 8)).astype(np.float32)
+    emb = rng.standard_normal((2, 12)).astype(np.float32)
+    out["rb_coords"], out["rb_features"], out["rb_emb"] = coords, feats, emb
+    x = L.SparseTensor(mx.array(feats), mx.array(coords))
+    plain = build("plain", 8, 16, 12)
+    y = plain(x, mx.array(emb))
+    out["plain_out"] = np.asarray(y.features, np.float32)
+    down = build("down", 16, 16, 12, downsample=True)
+    d = down(y, mx.array(emb))
+    out["down_coords"] = np.asarray(d.coords, np.int32)
+    out["down_out"] = np.asarray(d.features, np.float32)
+    up = build("up", 16, 8, 12, upsample=True)
+    u = up(d, mx.array(emb))
+    out["up_out"] = np.asarray(u.features, np.float32)
+    return out
+
+
 def topology_case(ref, reference_root: str) -> dict[str, np.ndarray]:
     _, L = ref
     mx = sys.modules["mlx.core"]
@@ -289,6 +367,9 @@ def main() -> None:
     path = os.path.join(HERE, "topology.npz")
     np.savez_compressed(path, **topology_case(ref, args.reference))
     print(f"topology -> {os.path.relpath(path, ROOT)}")
+    path = os.path.join(HERE, "resblock.npz")
+    np.savez_compressed(path, **resblock_case(ref, args.reference))
+    print(f"resblock -> {os.path.relpath(path, ROOT)}")
 
 
 if __name__ == "__main__":

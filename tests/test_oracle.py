@@ -145,3 +145,28 @@ def test_occupied_coordinates_match_reference(topology_golden):
     # threshold would list that cell
     unrounded = np.argwhere(half.astype(np.float64) > float(g["occ_half_threshold"]))
     assert len(unrounded) == len(g["occ_half_coords"]) + 1
+
+
+# ---- residual block --------------------------------------------------------------------------
+
+
+def resblock_params(g, prefix):
+    keys = ("norm1_w", "norm1_b", "conv1_w", "conv1_b", "conv2_w", "conv2_b", "emb_w", "emb_b",
+            "skip_w", "skip_b")
+    return {k: g[f"{prefix}_{k}"] for k in keys if f"{prefix}_{k}" in g}
+
+
+def test_resblock_matches_reference(resblock_golden):
+    g = resblock_golden
+    coords, feats, emb = g["rb_coords"], g["rb_features"], g["rb_emb"]
+    y = O.resblock(coords, feats, emb, resblock_params(g, "plain"))
+    np.testing.assert_allclose(y, g["plain_out"], rtol=1e-4, atol=1e-4)
+    # downsample block: pooled features of the plain block's output, on the coarse coords
+    dc, inv = O.downsample_coords(coords, 2)
+    assert np.array_equal(dc, g["down_coords"])
+    pooled = O.downsample_features(g["plain_out"], inv, len(dc))
+    d = O.resblock(dc, pooled, emb, resblock_params(g, "down"))
+    np.testing.assert_allclose(d, g["down_out"], rtol=1e-4, atol=1e-4)
+    # upsample block: the coarse output gathered back to the fine coords
+    u = O.resblock(coords, O.upsample_features(g["down_out"], inv), emb, resblock_params(g, "up"))
+    np.testing.assert_allclose(u, g["up_out"], rtol=1e-4, atol=1e-4)
