@@ -189,15 +189,17 @@ SV_API int sv_upsample_features(const void* coarse, int64_t m, int channels, int
 /* out[r] = act(mod(LayerNorm32(x[r]))) per row r of x [n, channels] (even, <= 4096):
  *   LayerNorm32: (x - mean) * rsqrt(mean((x - mean)^2) + eps), fp32, then * weight + bias when
  *     weight [channels] (fp32) is given (src/mlx_diffuser/layers/trellis.py:16-43);
- *   mod: * (1 + scale[b]) + shift[b] when scale / shift [batch, channels] (in `dtype`) are
+ *   mod: * (1 + scale[b]) + shift[b] when scale / shift (rows of `channels` values in `dtype`,
+ *     `mod_stride` elements apart -- e.g. the two halves of one [batch, 2C] projection; 0 =
+ *     one row shared by every batch element) are
  *     given, b = coords[r, 0] (the modulation of src/mlx_diffuser/models/trellis_slat.py:79);
  *   act: silu when `silu` is nonzero.
  * Computed in fp32 and rounded once to `dtype`; out may be x (in place). A batch index outside
  * [0, batch) ORs SV_DEVICE_BAD_INDEX into `status` and that row is not modulated. */
 SV_API int sv_rownorm(const void* x, int64_t n, int channels, int dtype, float eps,
                       const float* weight, const float* bias, const void* scale,
-                      const void* shift, const int32_t* coords, int64_t batch, int silu,
-                      void* out, int32_t* status, sv_stream_t stream);
+                      const void* shift, int64_t mod_stride, const int32_t* coords,
+                      int64_t batch, int silu, void* out, int32_t* status, sv_stream_t stream);
 
 /* ---- topology: occupancy -> coordinates, subdivision, attention windows --------------- */
 

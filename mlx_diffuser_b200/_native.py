@@ -67,7 +67,8 @@ _SIGNATURES = {
     "sv_weight_kio_to_oki": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P]),
     "sv_rownorm": (
         _I32,
-        [_P, _I64, _I32, _I32, ctypes.c_float, _P, _P, _P, _P, _P, _I64, _I32, _P, _P, _P],
+        [_P, _I64, _I32, _I32, ctypes.c_float, _P, _P, _P, _P, _I64, _P, _I64, _I32, _P, _P,
+         _P],
     ),
     "sv_downsample_workspace_bytes": (_SZ, [_I64]),
     "sv_downsample_coords": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _P, _P, _SZ, _P]),

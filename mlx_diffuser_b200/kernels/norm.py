@@ -40,7 +40,7 @@ def row_norm(
             raise ValueError(f"row_norm: weight must have shape ({c},)")
     if bias is not None:
         bias = bias.to(device=dev, dtype=torch.float32).contiguous()
-    mods = []
+    mods: list[torch.Tensor | None] = []
     for name, t in (("scale", scale), ("shift", shift)):
         if t is None:
             mods.append(None)
@@ -50,17 +50,24 @@ def row_norm(
             t = t[None]
         if t.ndim != 2 or t.shape[1] != c:
             raise ValueError(f"row_norm: {name} must have shape (B, {c})")
+        if t.stride(1) != 1 or (t.shape[0] > 1 and t.stride(0) < c):
+            t = t.contiguous()
         mods.append(t)
-    b = None
-    if any(m is not None for m in mods):
+    live = [m for m in mods if m is not None]
+    b = 0
+    mod_stride = 0
+    if live:
         if coords is None:
             raise ValueError("row_norm: modulation needs the coordinates (batch column)")
-        b = int(batch_size) if batch_size is not None else max(m.shape[0] for m in mods if m is not None)
-        mods = [None if m is None else (m.expand(b, c) if m.shape[0] == 1 else m).contiguous()
-                for m in mods]
-        for m in mods:
-            if m is not None and m.shape[0] != b:
-                raise ValueError(f"row_norm: modulation has {m.shape[0]} rows for batch {b}")
+        rows = {m.shape[0] for m in live}
+        b = int(batch_size) if batch_size is not None else max(rows)
+        if any(r not in (1, b) for r in rows):
+            raise ValueError(f"row_norm: modulation rows {sorted(rows)} for batch {b}")
+        strides = {0 if m.shape[0] == 1 else m.stride(0) for m in live}
+        if len(strides) > 1:  # scale and shift laid out differently: make both dense
+            mods = [None if m is None else m.expand(b, c).contiguous() for m in mods]
+            strides = {c}
+        mod_stride = strides.pop()
         coords = coords.to(device=dev, dtype=torch.int32).contiguous()
         if coords.shape != (n, 4):
             raise ValueError(f"row_norm: coords must have shape ({n}, 4)")
@@ -68,7 +75,8 @@ def row_norm(
         out = torch.empty_like(flat)
     rc = N.load().sv_rownorm(
         flat.data_ptr(), n, c, N.DTYPE_CODE[flat.dtype], float(eps), N.ptr(weight), N.ptr(bias),
-        N.ptr(mods[0]), N.ptr(mods[1]), N.ptr(coords), b or 0, int(bool(silu)), out.data_ptr(),
+        N.ptr(mods[0]), N.ptr(mods[1]), mod_stride, N.ptr(coords), b, int(bool(silu)),
+        out.data_ptr(),
         N.status_word(dev).data_ptr(), N.stream(dev),
     )
     N.check(rc, "row_norm")

@@ -70,6 +70,29 @@ def test_row_norm_matches_layernorm32(channels, dtype):
     N.check_device_status(DEV)
 
 
+@pytest.mark.parametrize("channels", [8, 64, 130, 1024])
+def test_row_norm_strided_and_shared_modulation(channels):
+    """scale / shift as the two halves of one [B, 2C] projection (row stride 2C, no copy) and
+    as one row shared by every batch element (row stride 0)."""
+
+    rng = np.random.default_rng(channels + 1)
+    dtype = torch.bfloat16
+    coords = scenes.batched([scenes.shell(12, 4.0, 2.0, 0.5, seed=s) for s in range(3)])
+    x = _rounded(rng.standard_normal((len(coords), channels)), dtype)
+    proj = _rounded(0.3 * rng.standard_normal((3, 2 * channels)), dtype)
+    scale, shift = torch.chunk(_t(proj, dtype), 2, dim=-1)
+    assert scale.stride(0) == 2 * channels
+    ct = _t(coords, torch.int32)
+    got = row_norm(_t(x, dtype), scale=scale, shift=shift, coords=ct, batch_size=3, silu=True)
+    bi = coords[:, 0]
+    ref = O.silu(O.layernorm32(x) * (1 + proj[bi, :channels]) + proj[bi, channels:])
+    assert max_rel_err(got.float().cpu().numpy(), ref) <= 8e-3
+    got = row_norm(_t(x, dtype), scale=scale[1:2], shift=shift[1], coords=ct, batch_size=3)
+    ref = O.layernorm32(x) * (1 + proj[1, :channels]) + proj[1, channels:]
+    assert max_rel_err(got.float().cpu().numpy(), ref) <= 8e-3
+    N.check_device_status(DEV)
+
+
 def test_row_norm_flags_bad_batch_index_and_rejects_bad_shapes():
     x = torch.randn((4, 16), device=DEV)
     coords = torch.tensor([[0, 0, 0, 0], [1, 0, 0, 1], [5, 0, 1, 0], [0, 1, 0, 0]],
@@ -204,3 +227,4 @@ def test_captured_resblock_stack_replays_bit_exactly():
     assert f"downsample_coords_2_{(1, 1, 1)}" in cache
     N.check_device_status(DEV)
     graphed.release()
+
