@@ -45,7 +45,8 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument(
         "--workload",
-        choices=["conv1024", "kmap", "pool", "scene128", "sweep", "halo", "topology", "resblock"],
+        choices=["conv1024", "kmap", "pool", "scene128", "sweep", "halo", "topology", "resblock",
+                 "backward"],
         default="conv1024",
         help="conv1024 (default): the headline line above. The others run on one GPU and "
         "print one line each: kmap = kernel-map build on 16 x 128^3 at 8%% occupancy; pool = "
@@ -56,7 +57,8 @@ def parse_args():
         "64->64->32 each after an NCCL halo exchange; topology = occupancy -> coords on 16 x 64^3 "
         "logits, sparse_subdivide and 8^3 attention windows of the 128^3 scene; resblock = the SLat "
         "I/O residual-block stack (128->128, 128->1024 down, 1024->128 up, 128->128) in fp16, "
-        "fused vs the reference's op-by-op sequence",
+        "fused vs the reference's op-by-op sequence; backward = input and weight gradients of "
+        "the headline conv (1024->1024 bf16 on 4 shells)",
     )
     p.add_argument(
         "--profiling",
@@ -680,6 +682,8 @@ def run_workload(args) -> None:
                                          "window grouping (key sort + first-row sort)")))
     elif args.workload == "resblock":
         lines.extend(resblock_lines(args, dev, flush))
+    elif args.workload == "backward":
+        lines.extend(backward_lines(args, dev, flush))
     for line in lines:
         print(json.dumps(line), flush=True)
     N.check_device_status(dev)
@@ -796,6 +800,70 @@ def resblock_lines(args, dev, flush) -> list:
         _line("residual-block stack voxels/s", n / (ms_ref * 1e-3), "voxels/s", ms_ref, args,
               dict(base, variant="reference op order (torch element-wise)"),
               {"bound": "tensor+hbm", "frac_of_roofline_time": roof_ms / ms_ref,
+               "peak_source": peaks["source"]}),
+    ]
+
+
+def backward_lines(args, dev, flush) -> list:
+    """Gradients of the headline convolution (4 shells at 32^3, 1024 -> 1024 bf16): the input
+    gradient (forward kernel over the same map with the flipped, transposed weight) and the
+    weight gradient (tcgen05 per-offset reduction over the pair lists). Each is 2*Cin*Cout*P
+    FLOPs; the pair lists and the flipped weight are built once, outside the timing."""
+
+    import torch
+
+    from mlx_diffuser_b200.kernels.sparse import (
+        conv3d_dgrad,
+        conv3d_wgrad,
+        kmap_pairs,
+        weight_flip_transpose,
+    )
+    from mlx_diffuser_b200 import _native as N
+    from mlx_diffuser_b200.kernels.sparse import conv3d_forward
+    from mlx_diffuser_b200.layers.sparse import build_neighbor_map, conv_row_order
+
+    coords_np, feats_np, weight_np = rank_inputs(0)
+    coords = torch.from_numpy(coords_np).to(dev)
+    feats = torch.from_numpy(feats_np).to(dev, torch.bfloat16)
+    weight = torch.from_numpy(weight_np).to(dev, torch.bfloat16).contiguous()
+    dout = torch.randn((len(coords_np), COUT), device=dev, dtype=torch.bfloat16)
+    nbr = build_neighbor_map(coords, 3)
+    ro, to = conv_row_order(nbr)
+    pairs = kmap_pairs(nbr)
+    p = int(pairs[1].numel())
+    w_t = weight_flip_transpose(weight)
+    ms_pairs = _time_device(lambda: kmap_pairs(nbr), args.steps, args.warmup, flush)
+    ms_flip = _time_device(lambda: weight_flip_transpose(weight), args.steps, args.warmup, flush)
+    ms_dgrad = _time_device(
+        lambda: conv3d_forward(dout, nbr, w_t, N.SV_WEIGHT_OKI, None, CIN, row_order=ro,
+                               tile_order=to), args.steps, args.warmup, flush)
+    ms_wgrad = _time_device(lambda: conv3d_wgrad(feats, dout, pairs, (3, 3, 3)), args.steps,
+                            args.warmup, flush)
+    ms_total = _time_device(
+        lambda: (conv3d_dgrad(dout, nbr, weight, unique=True, row_order=ro, tile_order=to),
+                 conv3d_wgrad(feats, dout, pairs, (3, 3, 3))), args.steps, args.warmup, flush)
+    N.check_device_status(dev)
+    peaks = measured_peaks()
+    flops = 2.0 * CIN * COUT * p
+
+    def roof(ms, kernel):
+        a = flops / (ms * 1e-3) / 1e12
+        return {"bound": "tensor", "kernel": kernel, "achieved": a, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": a / peaks["bf16_tflops"],
+                "peak_source": peaks["source"] + " (burst)", "flops_per_launch": flops}
+
+    base = {"workload": "shell32x4_conv1024_bf16_backward", "voxels": len(coords_np),
+            "valid_pairs": p, "pairs_build_ms": ms_pairs, "weight_flip_ms": ms_flip}
+    n = len(coords_np)
+    return [
+        _line("conv input-gradient voxels/s", n / (ms_dgrad * 1e-3), "voxels/s", ms_dgrad, args,
+              dict(base, part="dgrad"), roof(ms_dgrad, "conv_tc_kernel<256, 64, bf16> (W')")),
+        _line("conv weight-gradient voxels/s", n / (ms_wgrad * 1e-3), "voxels/s", ms_wgrad, args,
+              dict(base, part="wgrad"), roof(ms_wgrad, "wgrad_tc_kernel<256, bf16>")),
+        _line("conv backward voxels/s", n / (ms_total * 1e-3), "voxels/s", ms_total, args,
+              dict(base, part="dgrad (incl. weight flip) + wgrad"),
+              {"bound": "tensor", "frac_of_roofline_time":
+               2 * flops / (peaks["bf16_tflops"] * 1e12) / (ms_total * 1e-3),
                "peak_source": peaks["source"]}),
     ]
 

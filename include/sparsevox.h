@@ -184,6 +184,47 @@ SV_API int sv_upsample_features(const void* coarse, int64_t m, int channels, int
                                 const int32_t* inverse, int64_t n, void* out, int32_t* status,
                                 sv_stream_t stream);
 
+/* ---- backward (the gradients MLX takes through src/mlx_diffuser/kernels/sparse.py:39-55) -- */
+
+/* Pair lists of a kernel map: for each offset k, the pairs (src = nbr[p, k], dst = p) with
+ * nbr[p, k] >= 0, destinations ascending; offsets [kvol + 1] delimit the offsets' runs in
+ * pair_src / pair_dst [total]. Two calls on one workspace (sv_kmap_pairs_workspace_bytes):
+ * sv_kmap_pairs_count writes the number of pairs to *out_total (host memory; synchronises
+ * `stream`); sv_kmap_pairs_emit then fills the lists from the same map. */
+SV_API size_t sv_kmap_pairs_workspace_bytes(int64_t n, int kvol);
+SV_API int sv_kmap_pairs_count(const int32_t* nbr, int64_t n, int kvol, int64_t* out_total,
+                               void* workspace, size_t workspace_bytes, int32_t* status,
+                               sv_stream_t stream);
+SV_API int sv_kmap_pairs_emit(const int32_t* nbr, int64_t n, int kvol, int32_t* offsets,
+                              int32_t* pair_src, int32_t* pair_dst, int64_t total,
+                              void* workspace, size_t workspace_bytes, int32_t* status,
+                              sv_stream_t stream);
+
+/* Input gradient through the forward convolution: W'[i][j][o] = W[o][K-1-j][i] (spconv layout
+ * in and out; w_oki [cout, kvol, cin] -> out [cin, kvol, cout]). For a map with unique
+ * coordinates, d features = sv_conv3d_forward(dOut, nbr, W'); nbr[p, k] == q exactly when
+ * nbr[q, K-1-k] == p because offset K-1-k negates offset k. */
+SV_API int sv_weight_flip_transpose(const void* w_oki, int cout, int kvol, int cin, int dtype,
+                                    void* out, sv_stream_t stream);
+
+/* Weight gradient dW[o][k][i] = sum over offset k's pairs of dOut[dst][o] * features[src][i],
+ * written in spconv's (Cout, K, Cin) layout in `dtype`, fp32 accumulation, one rounding.
+ * features [n, cin], dout [n, cout]; the pair lists come from sv_kmap_pairs_*. AUTO takes the
+ * tcgen05 kernel for fp16/bf16 with Cin % 64 == 0 and Cout % 128 == 0 (16-byte aligned), which
+ * needs sv_conv3d_wgrad_workspace_bytes() of workspace; otherwise the CUDA-core kernel. */
+SV_API size_t sv_conv3d_wgrad_workspace_bytes(int cin, int cout, int kvol, int dtype, int algo);
+SV_API int sv_conv3d_wgrad(const void* features, const void* dout, int cin, int cout, int kvol,
+                           const int32_t* offsets, const int32_t* pair_src,
+                           const int32_t* pair_dst, int dtype, void* dweight, int algo,
+                           void* workspace, size_t workspace_bytes, int32_t* status,
+                           sv_stream_t stream);
+
+/* Bias gradient: column sums of dout [n, channels] in fp32, in a fixed order (deterministic),
+ * rounded to `dtype`. Workspace: sv_conv3d_dbias_workspace_bytes(n, channels). */
+SV_API size_t sv_conv3d_dbias_workspace_bytes(int64_t n, int channels);
+SV_API int sv_conv3d_dbias(const void* dout, int64_t n, int channels, int dtype, void* dbias,
+                           void* workspace, size_t workspace_bytes, sv_stream_t stream);
+
 /* ---- residual-block row normalisation ------------------------------------------------- */
 
 /* out[r] = act(mod(LayerNorm32(x[r]))) per row r of x [n, channels] (even, <= 4096):

@@ -74,6 +74,16 @@ _SIGNATURES = {
     "sv_downsample_coords": (_I32, [_P, _I64, _I32, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "sv_downsample_features": (_I32, [_P, _I64, _I32, _I32, _P, _P, _I64, _P, _P]),
     "sv_upsample_features": (_I32, [_P, _I64, _I32, _I32, _P, _I64, _P, _P, _P]),
+    "sv_kmap_pairs_workspace_bytes": (_SZ, [_I64, _I32]),
+    "sv_kmap_pairs_count": (_I32, [_P, _I64, _I32, _P, _P, _SZ, _P, _P]),
+    "sv_kmap_pairs_emit": (_I32, [_P, _I64, _I32, _P, _P, _P, _I64, _P, _SZ, _P, _P]),
+    "sv_weight_flip_transpose": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P]),
+    "sv_conv3d_wgrad_workspace_bytes": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
+    "sv_conv3d_wgrad": (
+        _I32, [_P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _I32, _P, _SZ, _P, _P]
+    ),
+    "sv_conv3d_dbias_workspace_bytes": (_SZ, [_I64, _I32]),
+    "sv_conv3d_dbias": (_I32, [_P, _I64, _I32, _I32, _P, _P, _SZ, _P]),
     "sv_occupancy_workspace_bytes": (_SZ, [_P]),
     "sv_occupancy_count": (_I32, [_P, _I32, _P, _P, ctypes.c_double, _P, _P, _SZ, _P]),
     "sv_occupancy_emit": (_I32, [_P, _I32, _P, _P, ctypes.c_double, _P, _I64, _P, _P, _SZ, _P]),

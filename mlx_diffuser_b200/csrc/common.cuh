@@ -262,6 +262,21 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return smem_desc_kmajor(saddr, 2u, 128u);
 }
 
+// Shared-memory matrix descriptor for an MN-major operand in 128-byte swizzle atoms: an atom is
+// 8 K-rows of 128 bytes (64 consecutive 16-bit M- or N-elements per K-row, 16-byte chunks XORed
+// with the row index); atoms follow each other `lbo` bytes apart along M/N and `sbo` bytes
+// apart along K (one 8-row group to the next).
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t lbo,
+                                                       uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address, bits [0,14)
+  d |= (uint64_t)(lbo >> 4) << 16;           // leading byte offset: next atom along M/N
+  d |= (uint64_t)(sbo >> 4) << 32;           // stride byte offset: next 8-row group along K
+  d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
+  d |= (uint64_t)2u << 61;                   // 128-byte swizzle
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation, both operands K-major.
 __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int m, int n) {
   return (1u << 4)                                   // D format: f32
@@ -269,6 +284,12 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int m, int n) {
          | ((bf16 ? 1u : 0u) << 10)                  // B format
          | ((uint32_t)(n >> 3) << 17)                // N / 8
          | ((uint32_t)(m >> 4) << 24);               // M / 16
+}
+
+// The same with the operands' major-ness: bit 15 = A is MN-major, bit 16 = B is MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16_major(bool bf16, int m, int n, bool a_mn,
+                                                       bool b_mn) {
+  return idesc_f16(bf16, m, n) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16);
 }
 
 }  // namespace sv

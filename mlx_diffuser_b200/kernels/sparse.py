@@ -10,6 +10,8 @@ kernel (everything else). ``use_metal`` is accepted for signature compatibility;
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from .. import _native as N
@@ -133,3 +135,149 @@ def sparse_conv3d(
 
 
 __all__ = ["sparse_conv3d"]
+
+
+# ---- backward --------------------------------------------------------------------------------
+
+
+def kmap_pairs(neighbors: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Per-offset pair lists of a kernel map: ``(offsets [K+1], src [P], dst [P])`` with
+    ``src = nbr[dst, k]`` for the pairs of offset k in ``offsets[k]:offsets[k+1]``, destinations
+    ascending (``sv_kmap_pairs_count`` / ``sv_kmap_pairs_emit``; one host synchronisation)."""
+
+    N.require_cuda(neighbors, "neighbors")
+    nbr = neighbors.contiguous()
+    n, kvol = nbr.shape
+    dev = nbr.device
+    lib = N.load()
+    ws_bytes = lib.sv_kmap_pairs_workspace_bytes(n, kvol)
+    ws = N.workspace(ws_bytes, dev)
+    status = N.status_word(dev)
+    total = ctypes.c_int64(0)
+    rc = lib.sv_kmap_pairs_count(nbr.data_ptr(), n, kvol, ctypes.byref(total), ws.data_ptr(),
+                                 ws_bytes, status.data_ptr(), N.stream(dev))
+    N.check(rc, "kmap_pairs")
+    p = int(total.value)
+    offsets = torch.empty(kvol + 1, dtype=torch.int32, device=dev)
+    src = torch.empty(max(p, 1), dtype=torch.int32, device=dev)
+    dst = torch.empty(max(p, 1), dtype=torch.int32, device=dev)
+    rc = lib.sv_kmap_pairs_emit(nbr.data_ptr(), n, kvol, offsets.data_ptr(), src.data_ptr(),
+                                dst.data_ptr(), p, ws.data_ptr(), ws_bytes, status.data_ptr(),
+                                N.stream(dev))
+    N.check(rc, "kmap_pairs")
+    return offsets, src[:p], dst[:p]
+
+
+def weight_flip_transpose(weight: torch.Tensor) -> torch.Tensor:
+    """``W'[i, j, o] = W[o, K-1-j, i]`` for a spconv ``(O, kD, kH, kW, I)`` weight, returned as
+    ``(I, kD, kH, kW, O)``: the weight of the forward convolution that computes the input
+    gradient (``sv_weight_flip_transpose``)."""
+
+    N.require_cuda(weight, "weight")
+    w = weight.contiguous()
+    o, kd, kh, kw, i = w.shape
+    out = torch.empty((i, kd, kh, kw, o), dtype=w.dtype, device=w.device)
+    rc = N.load().sv_weight_flip_transpose(w.data_ptr(), o, kd * kh * kw, i,
+                                           N.DTYPE_CODE[w.dtype], out.data_ptr(),
+                                           N.stream(w.device))
+    N.check(rc, "weight_flip_transpose")
+    return out
+
+
+def conv3d_wgrad(features: torch.Tensor, dout: torch.Tensor,
+                 pairs: tuple[torch.Tensor, torch.Tensor, torch.Tensor], kernel_shape,
+                 *, algo: int = N.SV_CONV_AUTO) -> torch.Tensor:
+    """Weight gradient in spconv layout ``(Cout, kD, kH, kW, Cin)`` (``sv_conv3d_wgrad``)."""
+
+    offsets, src, dst = pairs
+    f = features.contiguous()
+    g = dout.contiguous().to(f.dtype)
+    cin, cout = f.shape[1], g.shape[1]
+    kvol = offsets.numel() - 1
+    dev = f.device
+    out = torch.empty((cout, *kernel_shape, cin), dtype=f.dtype, device=dev)
+    lib = N.load()
+    code = N.DTYPE_CODE[f.dtype]
+    ws_bytes = lib.sv_conv3d_wgrad_workspace_bytes(cin, cout, kvol, code, algo)
+    ws = N.workspace(ws_bytes, dev) if ws_bytes else None
+    rc = lib.sv_conv3d_wgrad(f.data_ptr(), g.data_ptr(), cin, cout, kvol, offsets.data_ptr(),
+                             src.data_ptr(), dst.data_ptr(), code, out.data_ptr(), algo,
+                             N.ptr(ws), ws_bytes, N.status_word(dev).data_ptr(), N.stream(dev))
+    N.check(rc, "conv3d_wgrad")
+    return out
+
+
+def conv3d_dbias(dout: torch.Tensor) -> torch.Tensor:
+    """Column sums of ``dout`` in a fixed order (``sv_conv3d_dbias``)."""
+
+    g = dout.contiguous()
+    n, c = g.shape
+    dev = g.device
+    out = torch.empty(c, dtype=g.dtype, device=dev)
+    lib = N.load()
+    ws_bytes = lib.sv_conv3d_dbias_workspace_bytes(n, c)
+    ws = N.workspace(ws_bytes, dev)
+    rc = lib.sv_conv3d_dbias(g.data_ptr(), n, c, N.DTYPE_CODE[g.dtype], out.data_ptr(),
+                             ws.data_ptr(), ws_bytes, N.stream(dev))
+    N.check(rc, "conv3d_dbias")
+    return out
+
+
+def conv3d_dgrad(dout: torch.Tensor, neighbors: torch.Tensor, weight: torch.Tensor, *,
+                 unique: bool, row_order=None, tile_order=None,
+                 algo: int = N.SV_CONV_AUTO) -> torch.Tensor:
+    """Input gradient: the forward convolution of ``dout`` over the same map with the
+    flipped, transposed weight. With duplicate coordinates (``unique=False``) the gradient
+    flows only into the row each coordinate resolves to (the largest duplicate): ``dout`` is
+    first summed into that row, and the other duplicates get zero."""
+
+    w_t = weight_flip_transpose(weight)
+    cin = weight.shape[-1]
+    g = dout.contiguous().to(weight.dtype)
+    n, kvol = neighbors.shape
+    center = kvol // 2
+    if not unique:
+        resolved = neighbors[:, center].long()
+        merged = torch.zeros(g.shape, dtype=torch.float32, device=g.device)
+        merged.index_add_(0, resolved, g.float())
+        g = merged.to(g.dtype)
+    dx = conv3d_forward(g, neighbors, w_t, N.SV_WEIGHT_OKI, None, cin, row_order=row_order,
+                        tile_order=tile_order, algo=algo)
+    if not unique:
+        own = resolved == torch.arange(n, device=g.device)
+        dx = dx * own[:, None].to(dx.dtype)
+    return dx
+
+
+class SparseConv3DFunction(torch.autograd.Function):
+    """Submanifold conv with the gradients of mlx_diffuser's fallback
+    (``src/mlx_diffuser/kernels/sparse.py:39-55``): input gradient through the transposed map,
+    weight gradient per offset from the pair lists, bias gradient as column sums."""
+
+    @staticmethod
+    def forward(ctx, features, weight, bias, neighbors, topology, algo):
+        row_order, tile_order = topology.schedule()
+        out = conv3d_forward(features.contiguous(), neighbors, weight.contiguous(),
+                             N.SV_WEIGHT_OKI, bias, weight.shape[0], row_order=row_order,
+                             tile_order=tile_order, algo=algo)
+        ctx.save_for_backward(features, weight)
+        ctx.neighbors = neighbors
+        ctx.topology = topology
+        ctx.algo = algo
+        ctx.has_bias = bias is not None
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        features, weight = ctx.saved_tensors
+        topo = ctx.topology
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            row_order, tile_order = topo.schedule()
+            dx = conv3d_dgrad(dout, ctx.neighbors, weight, unique=topo.unique(),
+                              row_order=row_order, tile_order=tile_order, algo=ctx.algo)
+        if ctx.needs_input_grad[1]:
+            dw = conv3d_wgrad(features, dout, topo.pairs(), weight.shape[1:4], algo=ctx.algo)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = conv3d_dbias(dout.to(weight.dtype))
+        return dx, dw, db, None, None, None

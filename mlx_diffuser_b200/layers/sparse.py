@@ -29,7 +29,7 @@ import torch
 from torch import nn
 
 from .. import _native as N
-from ..kernels.sparse import conv3d_forward
+from ..kernels.sparse import SparseConv3DFunction, conv3d_forward, kmap_pairs
 
 
 def _triple(value, what: str) -> tuple[int, int, int]:
@@ -239,6 +239,39 @@ def conv_row_order(neighbors: torch.Tensor) -> tuple[torch.Tensor | None, torch.
     return order, tiles
 
 
+class MapTopology:
+    """The products of one cached kernel map that the convolution and its gradients use, each
+    built on first use and kept in the SparseTensor cache next to the map: the row schedule
+    (``conv_rows_*``), the per-offset pair lists (``conv_pairs_*``) and whether every
+    coordinate is unique (``conv_unique_*``)."""
+
+    def __init__(self, cache: dict, suffix: str, neighbors: torch.Tensor):
+        self.cache = cache
+        self.suffix = suffix
+        self.neighbors = neighbors
+
+    def _get(self, name: str, build):
+        key = f"{name}_{self.suffix}"
+        if key not in self.cache:
+            self.cache[key] = build()
+        return self.cache[key]
+
+    def schedule(self):
+        return self._get("conv_rows", lambda: conv_row_order(self.neighbors))
+
+    def pairs(self):
+        return self._get("conv_pairs", lambda: kmap_pairs(self.neighbors))
+
+    def unique(self) -> bool:
+        def build():
+            n, kvol = self.neighbors.shape
+            center = self.neighbors[:, kvol // 2]
+            return bool((center == torch.arange(n, device=center.device,
+                                                dtype=center.dtype)).all().item())
+
+        return self._get("conv_unique", build)
+
+
 class _SparseConv3DCore(nn.Module):
     """Parameter holder matching spconv's ``(O, kD, kH, kW, I)`` layout
     (``src/mlx_diffuser/layers/sparse.py:178-193``): uniform init in ±1/sqrt(I*k^3), zero bias.
@@ -307,18 +340,36 @@ class SparseConv3D(nn.Module):
         """``residual`` (optional, ``[N, Cout]`` in the feature dtype) is added to the output in
         the convolution's epilogue: ``conv(x) + residual`` with one rounding."""
 
-        key = f"neighbors_{self.kernel_size}_{self.dilation}_{x.scale}"
+        suffix = f"{self.kernel_size}_{self.dilation}_{x.scale}"
+        key = f"neighbors_{suffix}"
         neighbors = x.cache.get(key)
         if neighbors is None:
             neighbors = build_neighbor_map(x.coords, self.kernel_size, self.dilation)
             x.cache[key] = neighbors
-        plan_key = f"conv_rows_{self.kernel_size}_{self.dilation}_{x.scale}"
-        if plan_key not in x.cache:
-            x.cache[plan_key] = conv_row_order(neighbors)
+        topology = MapTopology(x.cache, suffix, neighbors)
+        row_order, tile_order = topology.schedule()
         features = x.features
         if features.ndim != 2:
             raise ValueError(f"features must be 2D, got {tuple(features.shape)}")
         N.require_cuda(features, "features")
+        w_param = self.conv.weight
+        b_param = self.conv.bias if hasattr(self.conv, "bias") else self.conv._bias
+        if torch.is_grad_enabled() and (features.requires_grad or w_param.requires_grad
+                                        or b_param.requires_grad):
+            # training: differentiable casts, gradients from the library's backward kernels
+            weight = w_param.to(device=features.device, dtype=features.dtype)
+            bias = b_param.to(device=features.device, dtype=features.dtype)
+            if features.shape[1] != weight.shape[-1] or neighbors.shape[0] != features.shape[0]:
+                raise ValueError(
+                    "weights must have shape "
+                    f"({neighbors.shape[1]}, {features.shape[1]}, Cout), got "
+                    f"({self.kernel_size**3}, {weight.shape[-1]}, {weight.shape[0]})"
+                )
+            out = SparseConv3DFunction.apply(features, weight, bias, neighbors, topology,
+                                             self.algo)
+            if residual is not None:
+                out = out + residual
+            return x.replace(out)
         weight, bias = self._operands(features.device, features.dtype)
         o, _, _, _, i = weight.shape
         if features.shape[1] != i or neighbors.shape[0] != features.shape[0]:
@@ -327,7 +378,6 @@ class SparseConv3D(nn.Module):
                 f"({neighbors.shape[1]}, {features.shape[1]}, Cout), got "
                 f"({self.kernel_size**3}, {i}, {o})"
             )
-        row_order, tile_order = x.cache[plan_key]
         out = conv3d_forward(
             features.contiguous(), neighbors, weight, N.SV_WEIGHT_OKI, bias, o,
             row_order=row_order, tile_order=tile_order, algo=self.algo,
@@ -639,6 +689,7 @@ def occupied_coordinates(logits: torch.Tensor, threshold: float = 0.0) -> torch.
 
 
 __all__ = [
+    "MapTopology",
     "SparseConv3D",
     "SparseTensor",
     "WindowGroups",

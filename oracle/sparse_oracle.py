@@ -354,3 +354,28 @@ def resblock(coords, feats, emb, p: dict, *, nbr=None) -> np.ndarray:
     h = sparse_conv3d(silu(h), nbr, spconv_weight_to_kio(p["conv2_w"]), p["conv2_b"])
     skip = feats @ p["skip_w"].T + p["skip_b"] if "skip_w" in p else feats
     return (h + skip).astype(np.float32)
+
+
+# --------------------------------------------------------------------------------------------
+# gradients
+# --------------------------------------------------------------------------------------------
+
+
+def sparse_conv3d_grads(features, neighbors, weights, dout, *, accum=np.float32):
+    """Gradients of the fallback (``src/mlx_diffuser/kernels/sparse.py:39-55``) with respect to
+    features, the (K, Cin, Cout) weights and the bias, for an output gradient ``dout``:
+    d features[q] = sum over (p, k) with nbr[p, k] == q of dout[p] @ W[k]^T;
+    d W[k] = features[nbr[valid, k]]^T @ dout[valid]; d bias = sum over rows of dout."""
+
+    features = np.asarray(features, accum)
+    dout = np.asarray(dout, accum)
+    w = np.asarray(weights, accum)
+    nbr = np.asarray(neighbors)
+    dx = np.zeros_like(features)
+    dw = np.zeros_like(w)
+    for k in range(nbr.shape[1]):
+        valid = nbr[:, k] >= 0
+        src = nbr[valid, k]
+        np.add.at(dx, src, dout[valid] @ w[k].T)
+        dw[k] = features[src].T @ dout[valid]
+    return dx, dw, dout.sum(0)

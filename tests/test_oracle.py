@@ -170,3 +170,33 @@ def test_resblock_matches_reference(resblock_golden):
     # upsample block: the coarse output gathered back to the fine coords
     u = O.resblock(coords, O.upsample_features(g["down_out"], inv), emb, resblock_params(g, "up"))
     np.testing.assert_allclose(u, g["up_out"], rtol=1e-4, atol=1e-4)
+
+
+# ---- gradients ----------------------------------------------------------------------------------
+
+
+def test_gradient_oracle_matches_autograd_of_the_fallback(golden):
+    """The closed-form gradients equal torch autograd (float64) of the reference's fallback
+    formula, out = bias + sum_k (features[max(nbr, 0)] @ W[k]) * valid, duplicates included."""
+
+    import torch
+
+    name, g = golden
+    if len(g["coords"]) > 2500:
+        pytest.skip("small fixtures only")
+    nbr = g["nbr"]
+    w = O.spconv_weight_to_kio(g["weight"]).astype(np.float64)
+    f = torch.tensor(g["features"], dtype=torch.float64, requires_grad=True)
+    wt = torch.tensor(w, requires_grad=True)
+    b = torch.tensor(g["bias"], dtype=torch.float64, requires_grad=True)
+    nb = torch.from_numpy(nbr.astype(np.int64))
+    out = b.expand(len(nbr), -1)
+    for k in range(nbr.shape[1]):
+        valid = (nb[:, k] >= 0).to(torch.float64)[:, None]
+        out = out + (f[nb[:, k].clamp(min=0)] @ wt[k]) * valid
+    dout = np.random.default_rng(4).standard_normal(out.shape)
+    out.backward(torch.from_numpy(dout))
+    dx, dw, db = O.sparse_conv3d_grads(g["features"], nbr, w, dout, accum=np.float64)
+    np.testing.assert_allclose(dx, f.grad.numpy(), rtol=1e-10, atol=1e-10)
+    np.testing.assert_allclose(dw, wt.grad.numpy(), rtol=1e-10, atol=1e-10)
+    np.testing.assert_allclose(db, b.grad.numpy(), rtol=1e-10, atol=1e-10)
