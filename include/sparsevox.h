@@ -152,6 +152,36 @@ SV_API int sv_conv3d_forward_residual(const void* features, int64_t n, int cin,
                                       size_t workspace_bytes, int32_t* status,
                                       sv_stream_t stream);
 
+/* sv_conv3d_forward_residual over a subset of the output rows: rows [n_rows] lists the rows to
+ * compute, in schedule order (e.g. the rows of one partition sorted by sv_conv_plan of their
+ * map rows; -1 entries are padding), tile_order (nullable) its 128-row tiles; other rows of
+ * `out` are left untouched.
+ * Features, map and bounds checks still span all n rows. Used to convolve the rows whose
+ * neighbours are all local while a halo exchange is in flight. */
+SV_API int sv_conv3d_forward_rows(const void* features, int64_t n, int cin, const int32_t* nbr,
+                                  int kvol, const int32_t* rows, int64_t n_rows,
+                                  const int32_t* tile_order, const void* weight, int layout,
+                                  const void* bias, const void* residual, int cout, int dtype,
+                                  void* out, int algo, void* workspace, size_t workspace_bytes,
+                                  int32_t* status, sv_stream_t stream);
+
+/* sv_conv3d_forward_rows on the tcgen05 kernel (fp16/bf16, spconv weight layout) for a
+ * partitioned scene whose halo rows other GPUs push into `features` (sv_halo_push): the rows
+ * list holds the rows that read only local rows first, then -- from tile-order position
+ * halo_from_tile on -- the rows that read halo rows (entries -1 pad the first segment to whole
+ * 128-row tiles). The first item at or past that position waits, inside the kernel, until each
+ * of the flag_count <= 8 flags (this GPU's data flags, raised by sv_halo_signal) is >= epoch
+ * (system-scope acquire, at most 1 s per CTA; an expired wait ORs SV_DEVICE_WAIT_TIMEOUT into
+ * `status`, marking the output invalid, and the launch still completes). One launch thus
+ * overlaps the local rows' convolution with the peers' pushes. Workspace: 256 B. */
+SV_API int sv_conv3d_forward_halo(const void* features, int64_t n, int cin, const int32_t* nbr,
+                                  int kvol, const int32_t* rows, int64_t n_rows,
+                                  const int32_t* tile_order, int32_t halo_from_tile,
+                                  int64_t* const* flags, int flag_count, int64_t epoch,
+                                  const void* weight, const void* bias, const void* residual,
+                                  int cout, int dtype, void* out, void* workspace,
+                                  size_t workspace_bytes, int32_t* status, sv_stream_t stream);
+
 /* Repack a (K, Cin, Cout) weight into spconv's (Cout, K, Cin) layout. */
 SV_API int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int cout, int dtype,
                                 void* w_oki, sv_stream_t stream);
@@ -183,6 +213,33 @@ SV_API int sv_downsample_features(const void* features, int64_t n, int channels,
 SV_API int sv_upsample_features(const void* coarse, int64_t m, int channels, int dtype,
                                 const int32_t* inverse, int64_t n, void* out, int32_t* status,
                                 sv_stream_t stream);
+
+/* ---- halo exchange over NVLink peer memory (Morton-partitioned scenes) ---------------- */
+
+/* CUDA IPC: sv_ipc_handle gives the 64-byte handle of the allocation holding `ptr` and ptr's
+ * offset in it; a peer process opens it with sv_ipc_open (base address out; add the offset) and
+ * releases it with sv_ipc_close(base). */
+SV_API int sv_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+SV_API int sv_ipc_open(const void* handle, void** base_out);
+SV_API int sv_ipc_close(void* base);
+
+/* Push halo rows: for j < m, row rows[j] of `local` ([local_rows, row_bytes]) is stored into
+ * row dst_rows[j] of peer peers[j]'s buffer, whose (IPC-mapped) address is peer_bases[peers[j]]
+ * and whose row count is peer_rows[peers[j]] (host arrays of npeers <= 8 entries). rows /
+ * dst_rows / peers are device int32 arrays; an index outside its buffer is skipped and
+ * SV_DEVICE_BAD_INDEX is ORed into `status`. Each store is followed by a system-scope fence. */
+SV_API int sv_halo_push(const void* local, int64_t local_rows, int row_bytes,
+                        const int32_t* rows, const int32_t* dst_rows, const int32_t* peers,
+                        int64_t m, void* const* peer_bases, const int64_t* peer_rows, int npeers,
+                        int32_t* status, sv_stream_t stream);
+
+/* Flags (int64 device words, local or IPC-mapped): sv_halo_signal stores `value` into each of
+ * count <= 8 flags with a system-scope release; sv_halo_wait waits on the stream until every
+ * flag is >= value (system-scope acquire), for at most 2 s, after which it ORs
+ * SV_DEVICE_WAIT_TIMEOUT into `status` and returns. */
+SV_API int sv_halo_signal(int64_t* const* flags, int count, int64_t value, sv_stream_t stream);
+SV_API int sv_halo_wait(int64_t* const* flags, int count, int64_t value, int32_t* status,
+                        sv_stream_t stream);
 
 /* ---- backward (the gradients MLX takes through src/mlx_diffuser/kernels/sparse.py:39-55) -- */
 

@@ -64,6 +64,16 @@ _SIGNATURES = {
         [_P, _I64, _I32, _P, _I32, _P, _P, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _P, _SZ, _P,
          _P],
     ),
+    "sv_conv3d_forward_rows": (
+        _I32,
+        [_P, _I64, _I32, _P, _I32, _P, _I64, _P, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _P,
+         _SZ, _P, _P],
+    ),
+    "sv_conv3d_forward_halo": (
+        _I32,
+        [_P, _I64, _I32, _P, _I32, _P, _I64, _P, _I32, _P, _I32, _I64, _P, _P, _P, _I32, _I32,
+         _P, _P, _SZ, _P, _P],
+    ),
     "sv_weight_kio_to_oki": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P]),
     "sv_rownorm": (
         _I32,
@@ -84,6 +94,12 @@ _SIGNATURES = {
     ),
     "sv_conv3d_dbias_workspace_bytes": (_SZ, [_I64, _I32]),
     "sv_conv3d_dbias": (_I32, [_P, _I64, _I32, _I32, _P, _P, _SZ, _P]),
+    "sv_ipc_handle": (_I32, [_P, _P, _P]),
+    "sv_ipc_open": (_I32, [_P, _P]),
+    "sv_ipc_close": (_I32, [_P]),
+    "sv_halo_push": (_I32, [_P, _I64, _I32, _P, _P, _P, _I64, _P, _P, _I32, _P, _P]),
+    "sv_halo_signal": (_I32, [_P, _I32, _I64, _P]),
+    "sv_halo_wait": (_I32, [_P, _I32, _I64, _P, _P]),
     "sv_occupancy_workspace_bytes": (_SZ, [_P]),
     "sv_occupancy_count": (_I32, [_P, _I32, _P, _P, ctypes.c_double, _P, _P, _SZ, _P]),
     "sv_occupancy_emit": (_I32, [_P, _I32, _P, _P, ctypes.c_double, _P, _I64, _P, _P, _SZ, _P]),

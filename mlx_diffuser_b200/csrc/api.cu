@@ -90,6 +90,14 @@ extern "C" int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int co
   return transpose(w_kio, (int64_t)kvol * cin, cout, dtype_size(dtype), w_oki, to_stream(stream));
 }
 
+extern "C" int sv_conv3d_forward_rows(const void* features, int64_t n, int cin,
+                                      const int32_t* nbr, int kvol, const int32_t* rows,
+                                      int64_t n_rows, const int32_t* tile_order,
+                                      const void* weight, int layout, const void* bias,
+                                      const void* residual, int cout, int dtype, void* out,
+                                      int algo, void* workspace, size_t workspace_bytes,
+                                      int32_t* status, sv_stream_t stream);
+
 extern "C" int sv_conv3d_forward(const void* features, int64_t n, int cin, const int32_t* nbr,
                                  int kvol, const int32_t* row_order, const int32_t* tile_order,
                                  const void* weight,
@@ -108,6 +116,24 @@ extern "C" int sv_conv3d_forward_residual(const void* features, int64_t n, int c
                                           const void* residual, int cout, int dtype, void* out,
                                           int algo, void* workspace, size_t workspace_bytes,
                                           int32_t* status, sv_stream_t stream) {
+  return sv_conv3d_forward_rows(features, n, cin, nbr, kvol, row_order, n, tile_order, weight,
+                                layout, bias, residual, cout, dtype, out, algo, workspace,
+                                workspace_bytes, status, stream);
+}
+
+extern "C" int sv_conv3d_forward_rows(const void* features, int64_t n, int cin,
+                                      const int32_t* nbr, int kvol, const int32_t* rows,
+                                      int64_t n_rows, const int32_t* tile_order,
+                                      const void* weight, int layout, const void* bias,
+                                      const void* residual, int cout, int dtype, void* out,
+                                      int algo, void* workspace, size_t workspace_bytes,
+                                      int32_t* status, sv_stream_t stream) {
+  const int32_t* row_order = rows;
+  // a row list may be longer than n: -1 entries pad schedule segments to whole tiles
+  if (n_rows < 0 || n_rows > (int64_t)INT32_MAX - 256)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward_rows: bad n_rows");
+  if (n_rows != n && rows == nullptr)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward_rows: a row subset needs its row list");
   if (n < 0 || cin < 0 || cout < 0 || kvol < 1)
     SV_FAIL(SV_ERR_BAD_SHAPE, "sv_conv3d_forward: negative size or empty kernel");
   if (!valid_dtype(dtype)) SV_FAIL(SV_ERR_BAD_DTYPE, "sv_conv3d_forward: unknown dtype");
@@ -115,12 +141,12 @@ extern "C" int sv_conv3d_forward_residual(const void* features, int64_t n, int c
     SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward: unknown weight layout");
   if (algo != SV_CONV_AUTO && algo != SV_CONV_SIMT && algo != SV_CONV_TCGEN05)
     SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward: unknown algorithm");
-  if (n == 0 || cout == 0) return SV_OK;
+  if (n_rows == 0 || cout == 0) return SV_OK;
   if (!features || !nbr || !out || (!weight && cin > 0))
     SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward: null pointer");
   cudaStream_t s = to_stream(stream);
   ConvArgs a{features, n, cin, nbr, kvol, row_order, weight, layout, bias, cout, dtype, out,
-             status, residual};
+             status, residual, n_rows, INT32_MAX, 0, 0, nullptr};
   const bool use_tc = tc_path(a, algo) && aligned16(weight);
   if (algo == SV_CONV_TCGEN05 && !use_tc)
     SV_FAIL(SV_ERR_UNSUPPORTED,
@@ -141,4 +167,33 @@ extern "C" int sv_conv3d_forward_residual(const void* features, int64_t n, int c
   }
   // tile_order only makes sense together with the row schedule it was derived from
   return conv_tc_launch(a, row_order ? tile_order : nullptr, counter, s);
+}
+
+extern "C" int sv_conv3d_forward_halo(const void* features, int64_t n, int cin,
+                                      const int32_t* nbr, int kvol, const int32_t* rows,
+                                      int64_t n_rows, const int32_t* tile_order,
+                                      int32_t halo_from_tile, int64_t* const* flags,
+                                      int flag_count, int64_t epoch, const void* weight,
+                                      const void* bias, const void* residual, int cout,
+                                      int dtype, void* out, void* workspace,
+                                      size_t workspace_bytes, int32_t* status,
+                                      sv_stream_t stream) {
+  if (n_rows < 0 || n_rows > (int64_t)INT32_MAX - 256 || n < 0 || cin < 0 || cout < 0 ||
+      kvol < 1)
+    SV_FAIL(SV_ERR_BAD_SHAPE, "sv_conv3d_forward_halo: bad sizes");
+  if (!valid_dtype(dtype)) SV_FAIL(SV_ERR_BAD_DTYPE, "sv_conv3d_forward_halo: unknown dtype");
+  if (flag_count < 0 || flag_count > 8 || (flag_count > 0 && !flags))
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward_halo: 0 to 8 flags");
+  if (n_rows == 0 || cout == 0) return SV_OK;
+  if (!features || !nbr || !out || !weight || !rows)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward_halo: null pointer");
+  ConvArgs a{features, n, cin, nbr, kvol, rows, weight, SV_WEIGHT_OKI, bias, cout, dtype, out,
+             status, residual, n_rows, halo_from_tile, flag_count, epoch, flags};
+  if (!tc_path(a, SV_CONV_TCGEN05) || !aligned16(weight))
+    SV_FAIL(SV_ERR_UNSUPPORTED,
+            "sv_conv3d_forward_halo runs on the tcgen05 kernel: fp16/bf16, Cin % 32 == 0, "
+            "Cout % 32 == 0, 16-byte aligned operands");
+  if (workspace == nullptr || workspace_bytes < 256 || !aligned16(workspace))
+    SV_FAIL(SV_ERR_WORKSPACE, "sv_conv3d_forward_halo: needs 256 bytes of workspace");
+  return conv_tc_launch(a, tile_order, static_cast<int32_t*>(workspace), to_stream(stream));
 }

@@ -20,6 +20,13 @@ struct ConvArgs {
   void* out;                 // [n, cout]
   int32_t* status;           // device status word or null
   const void* residual;      // [n, cout] added before rounding, or null; may equal `out`
+  int64_t n_rows;            // output rows to compute: row_order[0 .. n_rows) (n when no list)
+  // Halo rows written by other GPUs: tiles at tile-order positions >= wait_from are staged only
+  // after every one of the wait_count flags has reached wait_epoch (tcgen05 kernel only).
+  int32_t wait_from;         // INT32_MAX: nothing to wait for
+  int32_t wait_count;
+  int64_t wait_epoch;
+  int64_t* const* wait_flags;
 };
 
 // CUDA-core kernel: any dtype, shape and layout.

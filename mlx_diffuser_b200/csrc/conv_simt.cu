@@ -19,7 +19,8 @@ constexpr int SBM = 64, SBN = 64, SBK = 16;
 
 template <typename T, int LAYOUT>
 __global__ void __launch_bounds__(256) conv_simt_kernel(
-    const T* __restrict__ feat, int64_t n, int cin, const int32_t* __restrict__ nbr, int kvol,
+    const T* __restrict__ feat, int64_t n, int64_t n_rows, int cin,
+    const int32_t* __restrict__ nbr, int kvol,
     const int32_t* __restrict__ row_order, const T* __restrict__ w, const T* __restrict__ bias,
     const T* residual, int cout, T* out, int32_t* status) {
   __shared__ __align__(16) float As[SBK][SBM];
@@ -33,9 +34,9 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(
   if (tid < SBM) {
     const int64_t g = row0 + tid;
     int32_t o = -1;
-    if (g < n) {
+    if (g < n_rows) {
       o = row_order ? __ldg(&row_order[g]) : (int32_t)g;
-      if (o < 0 || o >= n) {
+      if (o < -1 || o >= n) {  // -1: padding between schedule segments
         report(status, SV_DEVICE_BAD_INDEX);
         o = -1;
       }
@@ -123,18 +124,18 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(
 
 template <typename T>
 int launch_typed(const ConvArgs& a, cudaStream_t s) {
-  const dim3 grid((unsigned)((a.n + SBM - 1) / SBM), (unsigned)((a.cout + SBN - 1) / SBN));
+  const dim3 grid((unsigned)((a.n_rows + SBM - 1) / SBM), (unsigned)((a.cout + SBN - 1) / SBN));
   const T* f = static_cast<const T*>(a.features);
   const T* w = static_cast<const T*>(a.weight);
   const T* b = static_cast<const T*>(a.bias);
   const T* r = static_cast<const T*>(a.residual);
   T* o = static_cast<T*>(a.out);
   if (a.layout == SV_WEIGHT_KIO)
-    conv_simt_kernel<T, SV_WEIGHT_KIO><<<grid, 256, 0, s>>>(f, a.n, a.cin, a.nbr, a.kvol,
+    conv_simt_kernel<T, SV_WEIGHT_KIO><<<grid, 256, 0, s>>>(f, a.n, a.n_rows, a.cin, a.nbr, a.kvol,
                                                             a.row_order, w, b, r, a.cout, o,
                                                             a.status);
   else
-    conv_simt_kernel<T, SV_WEIGHT_OKI><<<grid, 256, 0, s>>>(f, a.n, a.cin, a.nbr, a.kvol,
+    conv_simt_kernel<T, SV_WEIGHT_OKI><<<grid, 256, 0, s>>>(f, a.n, a.n_rows, a.cin, a.nbr, a.kvol,
                                                             a.row_order, w, b, r, a.cout, o,
                                                             a.status);
   SV_LAUNCH_CHECK();
@@ -144,8 +145,8 @@ int launch_typed(const ConvArgs& a, cudaStream_t s) {
 }  // namespace
 
 int conv_simt_launch(const ConvArgs& a, cudaStream_t s) {
-  if (a.n == 0 || a.cout == 0) return SV_OK;
-  if ((a.n + SBM - 1) / SBM > INT32_MAX || (a.cout + SBN - 1) / SBN > 65535)
+  if (a.n_rows == 0 || a.cout == 0) return SV_OK;
+  if ((a.n_rows + SBM - 1) / SBM > INT32_MAX || (a.cout + SBN - 1) / SBN > 65535)
     SV_FAIL(SV_ERR_UNSUPPORTED, "conv: problem too large for the grid");
   switch (a.dtype) {
     case SV_FLOAT32: return launch_typed<float>(a, s);

@@ -113,9 +113,35 @@ struct Sched {
   int32_t* counter;           // zeroed before the launch
   const int32_t* tile_order;  // row tiles, most expensive first (nullable: identity)
   int32_t row_tiles;
+  int32_t n_rows;             // rows of the schedule (row_order[0 .. n_rows)); -1 = padding
   int32_t n_tiles;            // Cout / BN
   int32_t total_items;        // row_tiles * n_tiles; order: n-slab major, then tile_order
+  int32_t wait_from;          // tile-order position of the first tile that reads halo rows
+  int32_t wait_count;         // flags to wait for before staging such a tile
+  int64_t wait_epoch;
+  int64_t* wait_flags[8];
 };
+
+// The halo rows other GPUs push into this GPU's buffer are complete once each of their flags
+// has reached the epoch (system-scope acquire, pairs with the pushers' release). Bounded by 1 s:
+// the other roles' waits for the next work item are bounded by 2 s, so this wait always gives up
+// first and the launch completes without tripping the abort path.
+__device__ __forceinline__ bool wait_halo_flags(const Sched& sc, volatile int* abort) {
+  const uint64_t t0 = global_timer_ns();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i >= sc.wait_count) break;
+    for (;;) {
+      int64_t v;
+      asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(sc.wait_flags[i])
+                   : "memory");
+      if (v >= sc.wait_epoch) break;
+      if (*abort || global_timer_ns() - t0 > 1000000000ull) return false;
+      __nanosleep(100);
+    }
+  }
+  return true;
+}
 
 template <int BN>
 __device__ __forceinline__ void decode_item(const Sched& sc, int32_t item, int32_t* row_tile,
@@ -387,9 +413,21 @@ __global__ void __launch_bounds__(TTHREADS, 1)
   } else {
     // ---- stagers: next work item, its rows and their neighbour lists (one row each) ----
     const int r = threadIdx.x - 320;
+    bool halo_ready = sc.wait_count == 0;
     for (int local = 0;; ++local) {
       const int ws = local & 1;
-      if (r == 0) *s_fetch = atomicAdd(sc.counter, 1);
+      if (r == 0) {
+        const int32_t fetched = atomicAdd(sc.counter, 1);
+        *s_fetch = fetched;
+        // the first item whose rows read halo rows waits for the peers' pushes; an expired
+        // wait is reported (the output is invalid) and the launch completes normally -- it does
+        // not abort, so no copy is ever left in flight
+        if (!halo_ready && fetched < sc.total_items &&
+            fetched % sc.row_tiles >= sc.wait_from) {
+          if (!wait_halo_flags(sc, s_abort)) report(status, SV_DEVICE_WAIT_TIMEOUT);
+          halo_ready = true;
+        }
+      }
       // the fetched item is visible, every stager is done with the previous one, and a stager
       // whose wait expired makes all of them leave together
       if (stager_bar_any(!ok)) {
@@ -408,9 +446,9 @@ __global__ void __launch_bounds__(TTHREADS, 1)
       if (valid && slot_free) {
         const int64_t gr = (int64_t)row_tile * TBM + r;
         int32_t orow = -1;
-        if (gr < n) {
+        if (gr < sc.n_rows) {
           orow = row_order ? __ldg(&row_order[gr]) : (int32_t)gr;
-          if (orow < 0 || orow >= n) {
+          if (orow < -1 || orow >= n) {  // -1: padding between schedule segments
             report(status, SV_DEVICE_BAD_INDEX);
             orow = -1;
           }
@@ -513,7 +551,12 @@ int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cu
   Sched sc;
   sc.counter = counter;
   sc.tile_order = tile_order;
-  sc.row_tiles = (int32_t)((a.n + TBM - 1) / TBM);
+  sc.row_tiles = (int32_t)((a.n_rows + TBM - 1) / TBM);
+  sc.n_rows = (int32_t)a.n_rows;
+  sc.wait_from = a.wait_count > 0 ? a.wait_from : INT32_MAX;
+  sc.wait_count = a.wait_count;
+  sc.wait_epoch = a.wait_epoch;
+  for (int i = 0; i < 8; ++i) sc.wait_flags[i] = i < a.wait_count ? a.wait_flags[i] : nullptr;
   sc.n_tiles = a.cout / BN;
   const int64_t items = (int64_t)sc.row_tiles * sc.n_tiles;
   if (items > INT32_MAX / 2) SV_FAIL(SV_ERR_UNSUPPORTED, "too many tensor-core work items");
@@ -562,10 +605,12 @@ bool conv_tc_supported(const ConvArgs& a) {
 
 int conv_tc_launch(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
                    cudaStream_t s) {
-  if (a.n == 0) return SV_OK;
+  if (a.n_rows == 0) return SV_OK;
   if (!conv_tc_supported(a))
     SV_FAIL(SV_ERR_UNSUPPORTED, "shape not supported by the tcgen05 kernel");
   if (counter == nullptr) SV_FAIL(SV_ERR_WORKSPACE, "tcgen05 conv needs a scheduler word");
+  if (a.wait_count < 0 || a.wait_count > 8 || (a.wait_count > 0 && a.wait_flags == nullptr))
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "tcgen05 conv: at most 8 halo flags");
   if (a.dtype == SV_BFLOAT16) return launch_typed<__nv_bfloat16>(a, tile_order, counter, s);
   return launch_typed<__half>(a, tile_order, counter, s);
 }

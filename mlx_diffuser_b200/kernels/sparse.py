@@ -45,11 +45,14 @@ def conv3d_forward(
     algo: int = N.SV_CONV_AUTO,
     out: torch.Tensor | None = None,
     residual: torch.Tensor | None = None,
+    rows: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Call ``sv_conv3d_forward_residual``. Tensors must already be contiguous, on one CUDA
     device, and share the feature dtype (``neighbors`` int32); ``layout`` is SV_WEIGHT_KIO or
     _OKI. ``row_order`` / ``tile_order`` are the schedule from :func:`conv_row_order`.
-    ``residual`` ([n, cout], optional, may be ``out``) is added to the result before rounding."""
+    ``residual`` ([n, cout], optional, may be ``out``) is added to the result before rounding.
+    ``rows`` (int32, optional) restricts the output to those rows, computed in that order with
+    ``tile_order`` as its tile schedule; the other rows of ``out`` are left untouched."""
 
     n, cin = features.shape
     kvol = neighbors.shape[1]
@@ -66,13 +69,18 @@ def conv3d_forward(
                                  or residual.dtype != features.dtype
                                  or not residual.is_contiguous()):
         raise ValueError(f"residual must be a contiguous ({n}, {cout}) {features.dtype} tensor")
-    rc = lib.sv_conv3d_forward_residual(
+    if rows is not None:
+        rows = rows.to(device=dev, dtype=torch.int32).contiguous()
+        if rows.numel() == 0:
+            return out
+    rc = lib.sv_conv3d_forward_rows(
         features.data_ptr(),
         n,
         cin,
         neighbors.data_ptr(),
         kvol,
-        N.ptr(row_order),
+        N.ptr(rows if rows is not None else row_order),
+        rows.numel() if rows is not None else n,
         N.ptr(tile_order),
         weight.data_ptr(),
         layout,
@@ -135,6 +143,26 @@ def sparse_conv3d(
 
 
 __all__ = ["sparse_conv3d"]
+
+
+def conv3d_forward_halo(features, neighbors, weight, bias, cout, rows, tile_order, halo_from,
+                        flags, flag_count, epoch, *, out, residual=None) -> torch.Tensor:
+    """``sv_conv3d_forward_halo``: one tcgen05 launch over ``rows`` whose tiles from tile-order
+    position ``halo_from`` on wait, inside the kernel, for ``flag_count`` peer flags (a ctypes
+    array of device pointers) to reach ``epoch``."""
+
+    n, cin = features.shape
+    dev = features.device
+    lib = N.load()
+    ws = N.workspace(256, dev)
+    rc = lib.sv_conv3d_forward_halo(
+        features.data_ptr(), n, cin, neighbors.data_ptr(), neighbors.shape[1], rows.data_ptr(),
+        rows.numel(), N.ptr(tile_order), int(halo_from), flags, int(flag_count), int(epoch),
+        weight.data_ptr(), N.ptr(bias), N.ptr(residual), cout, N.DTYPE_CODE[features.dtype],
+        out.data_ptr(), ws.data_ptr(), 256, N.status_word(dev).data_ptr(), N.stream(dev),
+    )
+    N.check(rc, "sparse_conv3d (halo)")
+    return out
 
 
 # ---- backward --------------------------------------------------------------------------------

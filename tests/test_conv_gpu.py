@@ -220,3 +220,97 @@ def test_conv_edge_cases():
     zero_out = sparse_conv3d(torch.zeros((3, cin), device=DEV), torch.zeros((3, 27), dtype=torch.int32),
                              torch.zeros((27, cin, 0)), torch.zeros(0))
     assert zero_out.shape == (3, 0)
+
+
+@pytest.mark.parametrize("algo", [N.SV_CONV_TCGEN05, N.SV_CONV_SIMT])
+def test_row_subset_conv_matches_full_conv_and_leaves_other_rows(algo):
+    """``rows=`` computes exactly those output rows (the halo overlap's interior and boundary
+    passes) with their own schedule, and leaves every other row of ``out`` untouched."""
+
+    from mlx_diffuser_b200.kernels.sparse import conv3d_forward
+    from mlx_diffuser_b200.layers.sparse import build_neighbor_map, conv_row_order
+
+    coords = scenes.shell32_batch(2)
+    dtype = torch.bfloat16
+    f = torch.from_numpy(scenes.normal_features(len(coords), 64, seed=5)).to(DEV, dtype)
+    w = torch.from_numpy(scenes.conv_weight(128, 64, 3, seed=6)).to(DEV, dtype).contiguous()
+    b = torch.linspace(-1, 1, 128, device=DEV).to(dtype)
+    nbr = build_neighbor_map(torch.from_numpy(coords).to(DEV), 3)
+    ro, to = conv_row_order(nbr)
+    full = conv3d_forward(f, nbr, w, N.SV_WEIGHT_OKI, b, 128, row_order=ro, tile_order=to,
+                          algo=algo)
+    subset = torch.from_numpy(np.random.default_rng(1).choice(len(coords), 5000,
+                                                              replace=False)).to(DEV)
+    sro, sto = conv_row_order(nbr[subset].contiguous())
+    rows = subset[sro.long()].to(torch.int32)
+    out = torch.full_like(full, 7.0)
+    conv3d_forward(f, nbr, w, N.SV_WEIGHT_OKI, b, 128, rows=rows, tile_order=sto, out=out,
+                   algo=algo)
+    assert torch.equal(out[subset], full[subset])
+    mask = torch.ones(len(coords), dtype=torch.bool, device=DEV)
+    mask[subset] = False
+    assert bool((out[mask] == 7.0).all())
+    N.check_device_status(DEV)
+
+
+def _fused_halo_case():
+    from mlx_diffuser_b200.layers.sparse import build_neighbor_map, conv_row_order
+
+    coords = scenes.shell32_batch(2)
+    n = len(coords)
+    f = torch.from_numpy(scenes.normal_features(n, 64, seed=8)).to(DEV, torch.bfloat16)
+    w = torch.from_numpy(scenes.conv_weight(64, 64, 3, seed=9)).to(DEV, torch.bfloat16).contiguous()
+    b = torch.linspace(-1, 1, 64, device=DEV).to(torch.bfloat16)
+    nbr = build_neighbor_map(torch.from_numpy(coords).to(DEV), 3)
+    perm = torch.from_numpy(np.random.default_rng(2).permutation(n)).to(DEV)
+    first, second = perm[: n // 3 * 2], perm[n // 3 * 2:]
+    segs = []
+    for sub in (first, second):
+        ro, to = conv_row_order(nbr[sub].contiguous())
+        segs.append((sub[ro.long()].to(torch.int32), to))
+    n_in = (segs[0][0].numel() + 127) // 128
+    pad = torch.full((n_in * 128 - segs[0][0].numel(),), -1, dtype=torch.int32, device=DEV)
+    rows = torch.cat([segs[0][0], pad, segs[1][0]])
+    tiles = torch.cat([segs[0][1], segs[1][1] + n_in]).to(torch.int32)
+    return f, nbr, w, b, rows, tiles, n_in
+
+
+def test_fused_halo_conv_with_raised_flag_matches_full_conv():
+    """One launch over [interior rows; padding; boundary rows] whose boundary tiles wait for a
+    data flag that is already raised: same output as the plain convolution."""
+
+    import ctypes
+
+    from mlx_diffuser_b200.kernels.sparse import conv3d_forward, conv3d_forward_halo
+
+    f, nbr, w, b, rows, tiles, n_in = _fused_halo_case()
+    full = conv3d_forward(f, nbr, w, N.SV_WEIGHT_OKI, b, 64)
+    flag = torch.full((1,), 5, dtype=torch.int64, device=DEV)
+    flags = (ctypes.c_void_p * 8)(flag.data_ptr())
+    out = torch.full_like(full, 3.0)
+    conv3d_forward_halo(f, nbr, w, b, 64, rows, tiles, n_in, flags, 1, 5, out=out)
+    assert torch.equal(out, full)
+    N.check_device_status(DEV)
+
+
+def test_fused_halo_conv_reports_an_expired_wait_and_stays_usable():
+    """A data flag that nothing raises: every waiting CTA gives up after its bounded wait, the
+    launch completes, the status word carries SV_DEVICE_WAIT_TIMEOUT, and the context keeps
+    working (a plain convolution afterwards is correct)."""
+
+    import ctypes
+
+    from mlx_diffuser_b200.kernels.sparse import conv3d_forward, conv3d_forward_halo
+
+    f, nbr, w, b, rows, tiles, n_in = _fused_halo_case()
+    flag = torch.zeros((1,), dtype=torch.int64, device=DEV)
+    flags = (ctypes.c_void_p * 8)(flag.data_ptr())
+    out = torch.empty((f.shape[0], 64), dtype=f.dtype, device=DEV)
+    conv3d_forward_halo(f, nbr, w, b, 64, rows, tiles, n_in, flags, 1, 1, out=out)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="timed out"):
+        N.check_device_status(DEV)
+    full = conv3d_forward(f, nbr, w, N.SV_WEIGHT_OKI, b, 64)
+    ref = conv3d_forward(f, nbr, w, N.SV_WEIGHT_OKI, b, 64, algo=N.SV_CONV_SIMT)
+    assert max_rel_err(full.float().cpu().numpy(), ref.float().cpu().numpy()) <= HALF_TOL
+    N.check_device_status(DEV)

@@ -109,3 +109,47 @@ def test_batch_shard_keeps_whole_elements_balanced():
                 elems = coords[p, 0].unique()
                 for e in elems:
                     assert int((coords[:, 0] == e).sum()) == int((coords[p, 0] == e).sum())
+
+
+def test_interior_boundary_split_covers_own_rows():
+    coords, _, _, _ = _scene()
+    nbr = torch.from_numpy(O.build_neighbor_map(coords, 3))
+    c = torch.from_numpy(coords)
+    for r in range(3):
+        plan = HaloPlan.build(c, nbr, r, 3)
+        interior, boundary = plan.split()
+        assert torch.equal(torch.sort(torch.cat([interior, boundary])).values,
+                           torch.arange(plan.num_own))
+        nb = plan.local_nbr
+        assert not bool((nb[interior] >= plan.num_own).any())
+        assert bool((nb[boundary] >= plan.num_own).any(dim=1).all())
+        assert interior.numel() > boundary.numel()  # Morton ranges keep most rows interior
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_peer_push_lists_fill_every_halo(world):
+    """Simulate the NVLink push on CPU: every rank stores its rows where push_lists says, and
+    each rank's halo block then equals the rows the NCCL exchange would deliver."""
+
+    from mlx_diffuser_b200.distributed import push_lists
+
+    coords, feats, _, _ = _scene()
+    nbr = torch.from_numpy(O.build_neighbor_map(coords, 3))
+    c = torch.from_numpy(coords)
+    f = torch.from_numpy(feats)
+    plans = [HaloPlan.build(c, nbr, r, world) for r in range(world)]
+    locals_ = []
+    for p in plans:
+        buf = torch.full((p.num_local, f.shape[1]), float("nan"))
+        buf[: p.num_own] = f[p.own]
+        locals_.append(buf)
+    num_own = [p.num_own for p in plans]
+    recv_off = [p.recv_offset for p in plans]
+    for s, p in enumerate(plans):
+        rows, dst, peers, receivers = push_lists(p, num_own, recv_off)
+        for j in range(rows.numel()):
+            r = receivers[int(peers[j])]
+            assert plans[r].num_own <= int(dst[j]) < plans[r].num_local  # only halo rows
+            locals_[r][int(dst[j])] = locals_[s][int(rows[j])]
+    for p, buf in zip(plans, locals_):
+        assert torch.equal(buf[p.num_own:], f[p.halo])

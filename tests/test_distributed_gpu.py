@@ -26,7 +26,13 @@ def _worker(rank: int, world: int, port: int, errors):
         from datetime import timedelta
 
         from mlx_diffuser_b200 import scenes
-        from mlx_diffuser_b200.distributed import HaloPlan, halo_conv
+        from mlx_diffuser_b200.distributed import (
+            HaloPlan,
+            PeerHalo,
+            halo_conv,
+            halo_conv_overlapped,
+            halo_conv_p2p,
+        )
         from mlx_diffuser_b200.kernels.sparse import conv3d_forward
         from mlx_diffuser_b200 import _native as N
         from mlx_diffuser_b200.layers.sparse import build_neighbor_map, conv_row_order
@@ -54,6 +60,24 @@ def _worker(rank: int, world: int, port: int, errors):
         ref = full[plan.own]
         err = (out_own.float() - ref.float()).abs().max() / ref.float().abs().max()
         assert float(err) <= 1e-6, float(err)
+        # the overlapped variant: interior rows while the exchange is in flight, then boundary
+        local2 = torch.zeros_like(local)
+        local2[: plan.num_own] = feats[plan.own]
+        out2 = halo_conv_overlapped(plan, local2, w, b)
+        assert torch.equal(local2[plan.num_own:], feats[plan.halo])
+        assert torch.equal(out2[: plan.num_own], out_own)
+        # NVLink peer-memory push: three exchanges in a row exercise the data / ack epochs
+        local3 = torch.zeros_like(local)
+        local3[: plan.num_own] = feats[plan.own]
+        halo = PeerHalo(plan, local3)
+        for _ in range(3):
+            out3 = halo_conv_p2p(halo, w, b)
+            torch.cuda.synchronize(dev)
+            assert torch.equal(local3[plan.num_own:], feats[plan.halo])
+            assert torch.equal(out3[: plan.num_own], out_own)
+        N.check_device_status(dev)
+        dist.barrier(device_ids=[rank])
+        halo.close()
         N.check_device_status(dev)
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
