@@ -108,6 +108,22 @@ SV_API int sv_kmap_build_static(const int32_t* coords, int64_t n, const int32_t 
                                 const int32_t dilation[3], int32_t* nbr, int32_t* status,
                                 sv_stream_t stream);
 
+/* The same map through a dense grid of row indices over the coordinates' bounding box instead
+ * of a hash table: one atomicMax per row, one load per neighbour. lo [4] is the box's minimum
+ * (batch, c1, c2, c3) and extent [4] its size (max - min + 1), e.g. from sv_coords_bounds; rows
+ * outside the box are not inserted and OR SV_DEVICE_BAD_INDEX into `status`. Workspace:
+ * sv_kmap_grid_workspace_bytes(extent) = 4 bytes per cell (0 for an invalid extent). Worth it
+ * when the box holds at most a few tens of cells per row. */
+/* sv_coords_bounds: bounds_out (host int32 [8]) = min then max of each coords column
+ * (synchronises `stream`; 32 bytes of workspace). */
+SV_API int sv_coords_bounds(const int32_t* coords, int64_t n, int32_t* bounds_out,
+                            void* workspace, size_t workspace_bytes, sv_stream_t stream);
+SV_API size_t sv_kmap_grid_workspace_bytes(const int64_t extent[4]);
+SV_API int sv_kmap_build_grid(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                              const int32_t dilation[3], int32_t* nbr, const int32_t lo[4],
+                              const int64_t extent[4], void* workspace, size_t workspace_bytes,
+                              int32_t* status, sv_stream_t stream);
+
 /* Schedule for the tensor-core convolution, derived from a kernel map:
  *  row_order [n]: a permutation of 0..n-1 that groups rows with equal neighbour-validity masks
  *                 (stable, so rows with one mask keep their spatial order);

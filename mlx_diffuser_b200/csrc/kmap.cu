@@ -127,6 +127,98 @@ __global__ void tile_cost_kernel(const uint32_t* __restrict__ masks_sorted, int6
   }
 }
 
+// ---- direct-indexed grid -------------------------------------------------------------------
+// When a scene's bounding box (in batch, c1, c2, c3) is not much larger than its row count, a
+// dense grid of row indices replaces the hash table: insert is one atomicMax per row (the
+// largest duplicate wins, as in the hash table and the reference's dict), a lookup is one
+// load, and the 3 offsets along c3 of a row hit neighbouring cells. Cells are row-major in
+// (batch, c1, c2, c3).
+
+struct GridBox {
+  int32_t lo[4];
+  int64_t ext[4];  // extents; cell = ((b * e1 + c1) * e2 + c2) * e3 + c3 after subtracting lo
+};
+
+__device__ __forceinline__ bool grid_cell(const GridBox& g, int64_t b, int64_t x, int64_t y,
+                                          int64_t z, int64_t* cell) {
+  b -= g.lo[0];
+  x -= g.lo[1];
+  y -= g.lo[2];
+  z -= g.lo[3];
+  if (b < 0 || b >= g.ext[0] || x < 0 || x >= g.ext[1] || y < 0 || y >= g.ext[2] || z < 0 ||
+      z >= g.ext[3])
+    return false;
+  *cell = ((b * g.ext[1] + x) * g.ext[2] + y) * g.ext[3] + z;
+  return true;
+}
+
+__global__ void bounds4_kernel(const int4* __restrict__ coords, int64_t n, int32_t* bounds) {
+  int mn[4] = {INT32_MAX, INT32_MAX, INT32_MAX, INT32_MAX};
+  int mx[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int4 c = __ldg(&coords[i]);
+    const int v[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      mn[j] = min(mn[j], v[j]);
+      mx[j] = max(mx[j], v[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    mn[j] = __reduce_min_sync(0xffffffffu, mn[j]);
+    mx[j] = __reduce_max_sync(0xffffffffu, mx[j]);
+  }
+  if ((threadIdx.x & 31) == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      atomicMin(&bounds[j], mn[j]);
+      atomicMax(&bounds[4 + j], mx[j]);
+    }
+  }
+}
+
+__global__ void bounds4_init_kernel(int32_t* bounds) {
+  if (threadIdx.x < 4) bounds[threadIdx.x] = INT32_MAX;
+  else if (threadIdx.x < 8) bounds[threadIdx.x] = INT32_MIN;
+}
+
+__global__ void grid_insert_kernel(const int4* __restrict__ coords, int64_t n, GridBox g,
+                                   int32_t* grid, int32_t* status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = __ldg(&coords[i]);
+  int64_t cell;
+  if (!grid_cell(g, c.x, c.y, c.z, c.w, &cell)) {
+    report(status, SV_DEVICE_BAD_INDEX);  // outside the box the caller gave: never written
+    return;
+  }
+  atomicMax(&grid[cell], (int32_t)i);
+}
+
+// One thread per (row, offset), like kmap_probe_kernel.
+__global__ void grid_probe_kernel(const int4* __restrict__ coords, int64_t n, GridBox g,
+                                  const int32_t* __restrict__ grid, int k0, int k1, int k2,
+                                  int d0, int d1, int d2, int32_t* __restrict__ nbr) {
+  const int kvol = k0 * k1 * k2;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * kvol) return;
+  const int64_t p = idx / kvol;
+  const int k = (int)(idx - p * kvol);
+  const int c = k % k2;
+  const int b = (k / k2) % k1;
+  const int a = k / (k1 * k2);
+  const int4 q = __ldg(&coords[p]);
+  int64_t cell;
+  int32_t r = -1;
+  if (grid_cell(g, q.x, (int64_t)q.y + (int64_t)(a - k0 / 2) * d0,
+                (int64_t)q.z + (int64_t)(b - k1 / 2) * d1,
+                (int64_t)q.w + (int64_t)(c - k2 / 2) * d2, &cell))
+    r = __ldg(&grid[cell]);
+  nbr[idx] = r;
+}
+
 size_t plan_cub_bytes(int64_t n) {
   size_t bytes = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
@@ -179,6 +271,83 @@ extern "C" int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t ker
   const int64_t total = n * kvol;
   kmap_probe_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, s>>>(
       reinterpret_cast<const int4*>(coords), n, table, mask, kernel[0], kernel[1], kernel[2],
+      dilation[0], dilation[1], dilation[2], nbr);
+  SV_LAUNCH_CHECK();
+  return SV_OK;
+}
+
+extern "C" int sv_coords_bounds(const int32_t* coords, int64_t n, int32_t* bounds_out,
+                                void* workspace, size_t workspace_bytes, sv_stream_t stream) {
+  if (n < 0 || !bounds_out) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_coords_bounds: bad arguments");
+  if (n == 0) {
+    for (int j = 0; j < 4; ++j) {
+      bounds_out[j] = 0;
+      bounds_out[4 + j] = -1;
+    }
+    return SV_OK;
+  }
+  if (!coords || !aligned16(coords))
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_coords_bounds: coords null or not 16-byte aligned");
+  if (!workspace || workspace_bytes < 32)
+    SV_FAIL(SV_ERR_WORKSPACE, "sv_coords_bounds: needs 32 bytes of workspace");
+  cudaStream_t s = to_stream(stream);
+  int32_t* dev_bounds = static_cast<int32_t*>(workspace);
+  bounds4_init_kernel<<<1, 32, 0, s>>>(dev_bounds);
+  SV_LAUNCH_CHECK();
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 4 * num_sms());
+  bounds4_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const int4*>(coords), n, dev_bounds);
+  SV_LAUNCH_CHECK();
+  SV_CUDA_TRY(cudaMemcpyAsync(bounds_out, dev_bounds, 8 * sizeof(int32_t),
+                              cudaMemcpyDeviceToHost, s));
+  SV_CUDA_TRY(cudaStreamSynchronize(s));
+  return SV_OK;
+}
+
+extern "C" size_t sv_kmap_grid_workspace_bytes(const int64_t extent[4]) {
+  if (!extent) return 0;
+  int64_t cells = 1;
+  for (int j = 0; j < 4; ++j) {
+    if (extent[j] <= 0) return 0;
+    if (cells > INT64_MAX / 4 / extent[j]) return 0;
+    cells *= extent[j];
+  }
+  return (size_t)cells * sizeof(int32_t);
+}
+
+extern "C" int sv_kmap_build_grid(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                                  const int32_t dilation[3], int32_t* nbr, const int32_t lo[4],
+                                  const int64_t extent[4], void* workspace,
+                                  size_t workspace_bytes, int32_t* status, sv_stream_t stream) {
+  if (n < 0 || kernel == nullptr || dilation == nullptr || lo == nullptr || extent == nullptr)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_kmap_build_grid: bad arguments");
+  for (int i = 0; i < 3; ++i)
+    if (kernel[i] <= 0 || kernel[i] % 2 == 0)
+      SV_FAIL(SV_ERR_BAD_SHAPE, "sparse submanifold kernels must have three odd dimensions");
+  const int64_t kvol = (int64_t)kernel[0] * kernel[1] * kernel[2];
+  if (n == 0) return SV_OK;
+  if (coords == nullptr || nbr == nullptr)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_kmap_build_grid: null coords or nbr");
+  if (n > INT32_MAX - 1) SV_FAIL(SV_ERR_UNSUPPORTED, "sv_kmap_build_grid: more than 2^31-2 rows");
+  if (!aligned16(coords)) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "coords must be 16-byte aligned");
+  const size_t need = sv_kmap_grid_workspace_bytes(extent);
+  if (need == 0) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_kmap_build_grid: bad extents");
+  if (workspace == nullptr || workspace_bytes < need)
+    SV_FAIL(SV_ERR_WORKSPACE, "sv_kmap_build_grid: workspace smaller than the grid");
+  GridBox g;
+  for (int j = 0; j < 4; ++j) {
+    g.lo[j] = lo[j];
+    g.ext[j] = extent[j];
+  }
+  cudaStream_t s = to_stream(stream);
+  int32_t* grid = static_cast<int32_t*>(workspace);
+  SV_CUDA_TRY(cudaMemsetAsync(grid, 0xFF, need, s));
+  const int threads = 256;
+  grid_insert_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, s>>>(
+      reinterpret_cast<const int4*>(coords), n, g, grid, status);
+  SV_LAUNCH_CHECK();
+  const int64_t total = n * kvol;
+  grid_probe_kernel<<<(unsigned)((total + threads - 1) / threads), threads, 0, s>>>(
+      reinterpret_cast<const int4*>(coords), n, g, grid, kernel[0], kernel[1], kernel[2],
       dilation[0], dilation[1], dilation[2], nbr);
   SV_LAUNCH_CHECK();
   return SV_OK;

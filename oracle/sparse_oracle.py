@@ -73,14 +73,15 @@ def build_neighbor_map_dict(coords, kernel_size, dilation=1) -> np.ndarray:
     return out
 
 
-_SPATIAL_BITS = 20  # packed key: batch 20 bits, each spatial column 20 bits (signed, biased)
+_SPATIAL_BITS = 20  # packed key: each spatial column 20 bits (signed, biased), batch 4 bits
 
 
 def build_neighbor_map(coords, kernel_size, dilation=1) -> np.ndarray:
     """Vectorised, bit-exact equivalent of :func:`build_neighbor_map_dict`.
 
-    Rows are packed into one int64 key when every coordinate, shifted by the largest offset,
-    fits in 20 signed bits and the batch index in [0, 2^20); otherwise the dict version runs.
+    Rows are packed into one 64-bit key when every coordinate, shifted by the largest offset,
+    fits in 20 signed bits and the batch index in the remaining 4 bits ([0, 16)); otherwise the
+    dict version runs.
     Duplicate rows resolve to the largest row index, which is what the reference's dict
     comprehension keeps (``src/mlx_diffuser/layers/sparse.py:159``).
     """
@@ -95,7 +96,7 @@ def build_neighbor_map(coords, kernel_size, dilation=1) -> np.ndarray:
     spatial = host[:, 1:].astype(np.int64)
     if (
         host[:, 0].min() < 0
-        or host[:, 0].max() >= (1 << _SPATIAL_BITS)
+        or host[:, 0].max() >= (1 << (64 - 3 * _SPATIAL_BITS))
         or spatial.min() < -lim
         or spatial.max() > lim
     ):

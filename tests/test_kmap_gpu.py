@@ -115,3 +115,58 @@ def test_conv_row_order_groups_rows_by_mask():
     assert all(a >= b for a, b in zip(cost, cost[1:]))
     assert conv_row_order(build_neighbor_map(torch.from_numpy(coords).to(DEV), 5)) == (None, None)
     N.check_device_status(DEV)
+
+
+# ---- dense-grid kernel map ----------------------------------------------------------------------
+
+
+def test_grid_map_matches_hash_map_on_every_fixture(golden):
+    """The grid path (forced) gives the hash path's map bit for bit: duplicates, negative
+    coordinates, three batch elements, anisotropic kernels and dilations."""
+
+    _, g = golden
+    coords = torch.from_numpy(g["coords"]).to(DEV)
+    maps = [(int(g["kernel_size"]), int(g["dilation"]), g["nbr"])]
+    i = 0
+    while f"nbr_extra{i}" in g:
+        maps.append((tuple(int(v) for v in g[f"nbr_extra{i}_kernel"]),
+                     tuple(int(v) for v in g[f"nbr_extra{i}_dilation"]), g[f"nbr_extra{i}"]))
+        i += 1
+    for ks, dl, want in maps:
+        got = build_neighbor_map(coords, ks, dl, method="grid")
+        assert np.array_equal(got.cpu().numpy(), want)
+        assert torch.equal(got, build_neighbor_map(coords, ks, dl, method="hash"))
+    N.check_device_status(DEV)
+
+
+def test_grid_map_auto_selection_on_dense_and_sparse_boxes():
+    dense = scenes.batched([scenes.uniform(64, 0.08, 700 + b) for b in range(4)])  # ~84k rows
+    c = torch.from_numpy(dense).to(DEV)
+    assert torch.equal(build_neighbor_map(c, 3, method="grid"),
+                       build_neighbor_map(c, 3, method="hash"))
+    assert torch.equal(build_neighbor_map(c, 3), build_neighbor_map(c, 3, method="hash"))
+    assert np.array_equal(build_neighbor_map(c, 3).cpu().numpy(), O.build_neighbor_map(dense, 3))
+    # far-apart batch indices make the box huge: auto keeps the hash table
+    sparse = dense.copy()
+    sparse[:, 0] *= 100000
+    c2 = torch.from_numpy(sparse).to(DEV)
+    assert np.array_equal(build_neighbor_map(c2, 3).cpu().numpy(), O.build_neighbor_map(sparse, 3))
+    N.check_device_status(DEV)
+
+
+def test_grid_map_refuses_rows_outside_the_given_box():
+    import ctypes
+
+    coords = torch.tensor([[0, 0, 0, 0], [0, 5, 5, 5], [0, 9, 9, 9]], dtype=torch.int32, device=DEV)
+    lib = N.load()
+    ext = (ctypes.c_int64 * 4)(1, 6, 6, 6)  # too small for the last row
+    ws = torch.empty(lib.sv_kmap_grid_workspace_bytes(ext), dtype=torch.uint8, device=DEV)
+    nbr = torch.empty((3, 27), dtype=torch.int32, device=DEV)
+    int3 = ctypes.c_int * 3
+    rc = lib.sv_kmap_build_grid(coords.data_ptr(), 3, int3(3, 3, 3), int3(1, 1, 1), nbr.data_ptr(),
+                                (ctypes.c_int32 * 4)(0, 0, 0, 0), ext, ws.data_ptr(), ws.numel(),
+                                N.status_word(DEV).data_ptr(), N.stream(DEV))
+    assert rc == N.SV_OK
+    with pytest.raises(RuntimeError, match="out of range"):
+        N.check_device_status(DEV)
+    assert int(nbr[0, 13]) == 0 and int(nbr[1, 13]) == 1 and int(nbr[2, 13]) == -1

@@ -200,3 +200,15 @@ def test_gradient_oracle_matches_autograd_of_the_fallback(golden):
     np.testing.assert_allclose(dx, f.grad.numpy(), rtol=1e-10, atol=1e-10)
     np.testing.assert_allclose(dw, wt.grad.numpy(), rtol=1e-10, atol=1e-10)
     np.testing.assert_allclose(db, b.grad.numpy(), rtol=1e-10, atol=1e-10)
+
+
+def test_vectorised_map_agrees_with_dict_map_for_large_batch_indices():
+    """The packed-key fast path keeps 4 bits for the batch index; larger indices take the dict
+    path (a guard that once let batch indices up to 2^20 into the 64-bit key collided)."""
+
+    rng = np.random.default_rng(3)
+    c = rng.integers(0, 6, size=(300, 4)).astype(np.int32)
+    for scale in (1, 5, 100000):
+        cc = c.copy()
+        cc[:, 0] = rng.integers(0, 4, size=300) * scale
+        assert np.array_equal(O.build_neighbor_map(cc, 3), O.build_neighbor_map_dict(cc, 3))
