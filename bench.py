@@ -46,7 +46,7 @@ def parse_args():
     p.add_argument(
         "--workload",
         choices=["conv1024", "kmap", "pool", "scene128", "sweep", "halo", "topology", "resblock",
-                 "backward"],
+                 "backward", "config1"],
         default="conv1024",
         help="conv1024 (default): the headline line above. The others run on one GPU and "
         "print one line each: kmap = kernel-map build on 16 x 128^3 at 8%% occupancy; pool = "
@@ -58,7 +58,8 @@ def parse_args():
         "logits, sparse_subdivide and 8^3 attention windows of the 128^3 scene; resblock = the SLat "
         "I/O residual-block stack (128->128, 128->1024 down, 1024->128 up, 128->128) in fp16, "
         "fused vs the reference's op-by-op sequence; backward = input and weight gradients of "
-        "the headline conv (1024->1024 bf16 on 4 shells)",
+        "the headline conv (1024->1024 bf16 on 4 shells); config1 = one fp32 conv 128->128 on a "
+        "~20k-voxel 64^3 shell (CUDA cores), with the CPU oracle timed beside it",
     )
     p.add_argument(
         "--profiling",
@@ -496,7 +497,7 @@ def run_ours(args) -> None:
             },
             "roofline": {
                 "bound": "tensor",
-                "kernel": "conv_tc_kernel<256, 64, bf16>",
+                "kernel": "conv_tc_kernel<256, 64, bf16, false>",
                 "achieved": achieved,
                 "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s",
@@ -716,6 +717,30 @@ def run_workload(args) -> None:
         lines.extend(resblock_lines(args, dev, flush))
     elif args.workload == "backward":
         lines.extend(backward_lines(args, dev, flush))
+    elif args.workload == "config1":
+        coords = scenes.shell64(0)
+        ms, pairs, x, _ = conv_case(coords, 128, 128, torch.float32, 21)
+        n = len(coords)
+        flops = 2.0 * 128 * 128 * pairs
+        # fp32 FFMA peak at the maximum SM clock: 148 SMs x 128 lanes x 2 FLOP
+        ffma_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        achieved = flops / (ms * 1e-3) / 1e12
+        # the reference's own algorithm on the host: dict map + gather-matmul fallback (fp32)
+        use_all_host_cores()
+        feats = scenes.normal_features(n, 128, 21)
+        from oracle import sparse_oracle as O
+
+        wk = O.spconv_weight_to_kio(scenes.conv_weight(128, 128, 3, 22))
+        t0 = time.perf_counter()
+        cpu_step(coords, feats, wk, np.zeros(128, np.float32))
+        cpu_s = time.perf_counter() - t0
+        lines.append(_line(
+            "sparse conv3d active-voxels/s", n / (ms * 1e-3), "voxels/s", ms, args,
+            {"workload": "shell64_conv128_fp32", "voxels": n, "valid_pairs": pairs,
+             "cpu_baseline_voxels_per_s": n / cpu_s, "cpu_cores": blas_threads()},
+            {"bound": "fp32 FFMA", "kernel": "conv_simt_kernel<float>", "achieved": achieved,
+             "peak": ffma_peak, "unit": "TFLOP/s", "frac": achieved / ffma_peak,
+             "peak_source": "148 SMs x 128 FP32 lanes x 2 x 1965 MHz (nominal)"}))
     for line in lines:
         print(json.dumps(line), flush=True)
     N.check_device_status(dev)
