@@ -295,6 +295,29 @@ class ClockSampler:
         }
 
 
+def bind_to_gpu_cpus(cuda_index: int) -> None:
+    """Restrict this process to the CPUs NVML lists as local to the GPU, so that its pinned host
+    buffers are first touched (and so allocated) on the GPU's own NUMA node. Used when several
+    ranks stream host data at once; a host without NVML keeps its affinity."""
+
+    try:
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        ncpu = os.cpu_count() or 64
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (ncpu + 63) // 64)
+        cpus = {64 * w + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
+        cpus &= set(range(ncpu))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+    except Exception:
+        pass
+
+
 def count_launches(step_fn) -> int | None:
     """Kernels one step launches, counted by the CUDA profiler on an extra untimed step."""
 
@@ -335,6 +358,7 @@ def run_ours(args) -> None:
     if world > 1:
         from datetime import timedelta
 
+        bind_to_gpu_cpus(local)
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     coords_np, feats_np, weight_np = rank_inputs(rank)
