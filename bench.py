@@ -104,10 +104,16 @@ def profiled_traffic() -> float | None:
 # ---------------------------------------------------------------------------------------------
 
 
-def use_all_host_cores() -> None:
-    """The CPU baseline runs on every host core: torchrun exports OMP_NUM_THREADS=1 to its
-    ranks, so lift the BLAS thread limit explicitly."""
+# The process's CPU set before bind_to_gpu_cpus narrowed it (None: never narrowed).
+_HOST_CPUS = None
 
+
+def use_all_host_cores() -> None:
+    """The CPU baseline runs on every host core: undo the GPU-local CPU binding, and, since
+    torchrun exports OMP_NUM_THREADS=1 to its ranks, lift the BLAS thread limit explicitly."""
+
+    if _HOST_CPUS:
+        os.sched_setaffinity(0, _HOST_CPUS)
     try:
         from threadpoolctl import threadpool_limits
 
@@ -297,9 +303,11 @@ class ClockSampler:
 
 def bind_to_gpu_cpus(cuda_index: int) -> None:
     """Restrict this process to the CPUs NVML lists as local to the GPU, so that its pinned host
-    buffers are first touched (and so allocated) on the GPU's own NUMA node. Used when several
-    ranks stream host data at once; a host without NVML keeps its affinity."""
+    buffers are first touched (and so allocated) on the GPU's own NUMA node: the e2e copies then
+    stay off the inter-socket link. A host without NVML keeps its affinity; use_all_host_cores
+    restores the full set for the CPU baseline."""
 
+    global _HOST_CPUS
     try:
         import pynvml
         import torch
@@ -308,11 +316,12 @@ def bind_to_gpu_cpus(cuda_index: int) -> None:
         uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
         uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
         handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
-        ncpu = os.cpu_count() or 64
-        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (ncpu + 63) // 64)
+        allowed = os.sched_getaffinity(0)
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (max(allowed) + 64) // 64)
         cpus = {64 * w + b for w, word in enumerate(words) for b in range(64) if (word >> b) & 1}
-        cpus &= set(range(ncpu))
-        if cpus:
+        cpus &= allowed
+        if cpus and cpus != allowed:
+            _HOST_CPUS = set(allowed)
             os.sched_setaffinity(0, cpus)
     except Exception:
         pass
@@ -355,10 +364,10 @@ def run_ours(args) -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    bind_to_gpu_cpus(local)
     if world > 1:
         from datetime import timedelta
 
-        bind_to_gpu_cpus(local)
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     coords_np, feats_np, weight_np = rank_inputs(rank)
