@@ -45,7 +45,7 @@ typedef enum sv_status {
   SV_ERR_BAD_DTYPE = 3,
   SV_ERR_TABLE_FULL = 4,       /* coordinate hash table too small for the input */
   SV_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed */
-  SV_ERR_UNSUPPORTED = 6,      /* valid input outside what this build implements */
+  SV_ERR_UNSUPPORTED = 6,      /* valid input outside what the library implements */
   SV_ERR_WORKSPACE = 7         /* workspace pointer null or smaller than required */
 } sv_status;
 
