@@ -11,6 +11,10 @@ kernel map (hash insert + 27-offset probe) and the row schedule, then the tensor
 
 With N > 1 it runs under torchrun, one rank per GPU; each rank convolves its own batch of 4
 shells (weak scaling, no communication on the data path) and rank 0 prints the JSON line.
+The same line carries, at every N, a ``halo`` block: the 237k-voxel 128^3 scene of config 4
+Morton-partitioned over the N ranks (strong scaling, NVLink halo push in one launch per layer,
+NCCL beside it, parity checked on the box); and at N = 1 a ``secondary`` block: configs 1, 3,
+4 and a bounded part of 5, each with its roofline fraction and CPU baseline.
 ``--impl reference`` times the reference's own algorithm (dict-based neighbour map and the
 gather-matmul fallback, restated in NumPy) on the host cores, on rank 0 only.
 """
@@ -46,7 +50,7 @@ def parse_args():
     p.add_argument(
         "--workload",
         choices=["conv1024", "kmap", "pool", "scene128", "sweep", "halo", "topology", "resblock",
-                 "backward", "config1"],
+                 "backward", "config1", "hbm"],
         default="conv1024",
         help="conv1024 (default): the headline line above. The others run on one GPU and "
         "print one line each: kmap = kernel-map build on 16 x 128^3 at 8%% occupancy; pool = "
@@ -59,7 +63,10 @@ def parse_args():
         "I/O residual-block stack (128->128, 128->1024 down, 1024->128 up, 128->128) in fp16, "
         "fused vs the reference's op-by-op sequence; backward = input and weight gradients of "
         "the headline conv (1024->1024 bf16 on 4 shells); config1 = one fp32 conv 128->128 on a "
-        "~20k-voxel 64^3 shell (CUDA cores), with the CPU oracle timed beside it",
+        "~20k-voxel 64^3 shell (CUDA cores), with the CPU oracle timed beside it; hbm = the "
+        "HBM-bound kernels once per step each through the package API (map and pooling on "
+        "4 x 128^3 at 8%% with 128 bf16 channels, row norm + SiLU on those rows at 1024 "
+        "channels, subdivide of the coarse tensor, occupancy of 16 x 64^3 fp32 logits)",
     )
     p.add_argument(
         "--profiling",
@@ -134,6 +141,29 @@ def blas_threads() -> int:
     return os.cpu_count() or 1
 
 
+def host_facts() -> dict:
+    """Where the CPU numbers were taken: the CPU model (from /proc/cpuinfo, what lscpu prints as
+    "Model name"), the logical CPU count, and whether MLX itself imports on this host (its CPU
+    backend would then be timed; mlx_diffuser pins mlx 0.31.2, which has no Linux wheel here)."""
+
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.lower().startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        import mlx.core  # noqa: F401
+
+        mlx = "importable"
+    except Exception as e:  # the expected case on this host
+        mlx = f"not importable: {type(e).__name__}: {e}"
+    return {"cpu_model": model, "cpu_count": os.cpu_count(), "mlx_core": mlx}
+
+
 def cpu_sample(rank: int = 0):
     """One bounded sample of the workload: the first of the rank's shells (about 6k voxels)."""
 
@@ -167,6 +197,7 @@ def cpu_baseline(reps: int = 2) -> dict:
         "value": len(coords) / t,
         "unit": UNIT,
         "cores": blas_threads(),
+        **host_facts(),
         "kind": "port",
         "sample": (
             f"1 of 4 shells ({len(coords)} voxels): dict neighbour map + the reference's "
@@ -214,6 +245,7 @@ def run_reference(args) -> None:
             "value": value,
             "unit": UNIT,
             "cores": blas_threads(),
+            **host_facts(),
             "kind": "port",
             "sample": (
                 f"1 of 4 shells ({len(coords)} voxels) per step: dict neighbour map + the "
@@ -487,6 +519,20 @@ def run_ours(args) -> None:
 
     launches = None if args.profiling else count_launches(mid_step)
 
+    # the host link's ceiling for the e2e traffic, every rank copying at once
+    barrier()
+    link = link_ceiling(coords_h, feats_h, out_h[0], y.features, c_d[0], f_d[0], dev)
+    link_t = torch.tensor([link["gbs"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(link_t, op=dist.ReduceOp.MIN)
+    link_gbs = float(link_t.item())
+
+    # config 4's partitioned scene over the same ranks (strong scaling, parity checked on the box)
+    halo = None if args.profiling else halo_measure(args, world, rank, local, dev)
+    secondary = None
+    if world == 1 and not args.profiling:
+        secondary = secondary_block(args, dev, flush)
+
     stats = torch.tensor([mean_step, mean_conv, mean_e2e, float(n), float(pairs)],
                          dtype=torch.float64, device=dev)
     if world > 1:
@@ -548,7 +594,15 @@ def run_ours(args) -> None:
                 "pipelining": "next step's H2D and previous step's D2H on copy streams, "
                               "overlapped with the current step's compute; no L2 flush (152 MB "
                               "per-step working set)",
+                "link_gbs_measured": link_gbs,
+                "link_frac": (coords_h.numel() * 4 + feats_h.numel() * 2 + out_h[0].numel() * 2)
+                             / (mean_e2e * 1e-3) / 1e9 / link_gbs,
+                "link": "pinned H2D of the step's inputs and D2H of its output, concurrently on "
+                        "two streams, on every rank at once (slowest rank); link_frac = the e2e "
+                        "step's bytes per second over that ceiling",
             },
+            "halo": halo,
+            "secondary": secondary,
             "gpu_launches": None if launches is None else launches * args.steps,
             "clocks": clocks,
         }
@@ -610,15 +664,349 @@ def _hbm_roofline(bytes_per_launch: float, ms: float, kernel: str) -> dict:
             "peak_source": peaks["source"], "algorithmic_bytes": bytes_per_launch}
 
 
+def conv_timing(args, dev, flush, coords, cin, cout, dtype, seed, feats=None):
+    """One cached-map convolution through ``SparseConv3D``: mean device ms, valid pairs, the
+    input tensor and its roofline (tensor or HBM bound, whichever is slower at the measured
+    peaks; F = 2 Cin Cout P, B = dt N (Cin + Cout) + dt K Cin Cout + 4 K N)."""
+
+    import torch
+
+    from mlx_diffuser_b200 import scenes
+    from mlx_diffuser_b200.layers.sparse import SparseConv3D, SparseTensor
+
+    n = len(coords)
+    c = torch.from_numpy(coords).to(dev)
+    if feats is None:
+        feats = torch.from_numpy(scenes.normal_features(n, cin, seed)).to(dev, dtype)
+    conv = SparseConv3D(cin, cout, 3).to(dev)
+    conv.conv.weight = torch.from_numpy(scenes.conv_weight(cout, cin, 3, seed + 1)).to(dev, dtype)
+    conv.conv.bias = torch.zeros(cout, device=dev, dtype=dtype)
+    x = SparseTensor(feats, c, int(coords[:, 0].max()) + 1, None)
+    conv(x)  # builds and caches the map and schedule
+    nbr = x.cache["neighbors_3_1_(1, 1, 1)"]
+    pairs = int((nbr >= 0).sum().item())
+    ms = _time_device(lambda: conv(x), args.steps, args.warmup, flush)
+    return ms, pairs, x, conv_roofline(n, cin, cout, pairs, dtype, ms)
+
+
+def conv_roofline(n, cin, cout, pairs, dtype, ms) -> dict:
+    import torch
+
+    flops = 2.0 * cin * cout * pairs
+    dsz = torch.finfo(dtype).bits // 8
+    bytes_ = dsz * n * (cin + cout) + dsz * 27 * cin * cout + 4 * 27 * n
+    peaks = measured_peaks()
+    t_tensor = flops / (peaks["bf16_tflops"] * 1e12)
+    t_hbm = bytes_ / (peaks["hbm_gbs"] * 1e9)
+    if t_tensor >= t_hbm:
+        roof = {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12,
+                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": bytes_ / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["roofline_ms"] = max(t_tensor, t_hbm) * 1e3
+    roof["frac_of_roofline_time"] = roof["roofline_ms"] / ms
+    roof["peak_source"] = peaks["source"]
+    return roof
+
+
+def map_timing(args, dev, flush, coords):
+    import torch
+
+    from mlx_diffuser_b200.layers.sparse import build_neighbor_map
+
+    c = torch.from_numpy(coords).to(dev)
+    n = len(coords)
+    ms = _time_device(lambda: build_neighbor_map(c, 3), args.steps, args.warmup, flush)
+    return ms, _hbm_roofline(16.0 * n + 4.0 * 27 * n, ms, "kmap_insert + kmap_probe")
+
+
+def cpu_conv_sample(coords, feats, w_kio, rows: int, seed: int = 0) -> dict:
+    """The reference's algorithm on the host for a bounded sample of ``rows`` output rows of a
+    scene: the dict of every coordinate row (timed once), the 27 lookups and the gather-matmul
+    fallback for the sampled rows (fp32, all BLAS threads). The rate is extrapolated to the
+    whole scene: N / (dict time + sample time * N / rows)."""
+
+    from oracle import sparse_oracle as O
+
+    use_all_host_cores()
+    n = len(coords)
+    sample = np.sort(np.random.default_rng(seed).choice(n, min(rows, n), replace=False))
+    host = np.asarray(coords, np.int32)
+    t0 = time.perf_counter()
+    lookup = {tuple(int(v) for v in row): i for i, row in enumerate(host)}
+    t_dict = time.perf_counter() - t0
+    offsets = O.kernel_offsets(3)
+    t0 = time.perf_counter()
+    nbr = np.full((len(sample), 27), -1, np.int32)
+    for i, p in enumerate(sample):
+        b, c1, c2, c3 = (int(v) for v in host[p])
+        for k, (d1, d2, d3) in enumerate(offsets):
+            nbr[i, k] = lookup.get((b, c1 + d1, c2 + d2, c3 + d3), -1)
+    O.sparse_conv3d_fallback_literal(feats, nbr, w_kio, np.zeros(w_kio.shape[2], np.float32))
+    t_sample = time.perf_counter() - t0
+    total = t_dict + t_sample * n / len(sample)
+    return {"value": n / total, "unit": "voxels/s", "cores": blas_threads(), "kind": "port",
+            "sample": f"dict of all {n} rows + lookups and fallback for {len(sample)} sampled "
+                      "rows, extrapolated to the scene"}
+
+
+def config3_stack(dev, dt):
+    """BASELINE config 3, the SLat flow's sparse I/O stack (fp16, batch 2, two ~20k-voxel 64^3
+    shells, 8 latent channels): residual block 8 -> 128 (SiLU(LN32) -> conv 8->128 ->
+    LN32 * (1 + scale) + shift -> SiLU -> conv 128->128, plus a 1x1 skip), downsample, conv
+    128 -> 1024, upsample, conv 1024 -> 128, conv 128 -> 8. Returns (run, conv specs, rows,
+    cpu_run): ``run()`` is the library path (torch for the dense glue), ``cpu_run(element)``
+    the same stack in the fp32 oracle on one batch element."""
+
+    import torch
+    import torch.nn.functional as F
+
+    from mlx_diffuser_b200 import scenes
+    from mlx_diffuser_b200.layers.sparse import (
+        SparseConv3D,
+        SparseTensor,
+        sparse_downsample,
+        sparse_upsample,
+    )
+    from oracle import sparse_oracle as O
+
+    rng = np.random.default_rng(30)
+    per = [scenes.shell64(3), scenes.shell64(4)]
+    coords = scenes.batched(per)
+    n = len(coords)
+    x0 = scenes.normal_features(n, 8, seed=31)
+    specs = {"c1": (8, 128), "c2": (128, 128), "c3": (128, 1024), "c4": (1024, 128),
+             "c5": (128, 8)}
+    ws = {k: scenes.conv_weight(co, ci, 3, 32 + i) for i, (k, (ci, co)) in enumerate(specs.items())}
+    bs = {k: (rng.standard_normal(w.shape[0]) * 0.05).astype(np.float32) for k, w in ws.items()}
+    skip_w = (rng.standard_normal((128, 8)) / np.sqrt(8)).astype(np.float32)
+    skip_b = (rng.standard_normal(128) * 0.05).astype(np.float32)
+    scale = (rng.standard_normal((2, 128)) * 0.1).astype(np.float32)
+    shift = (rng.standard_normal((2, 128)) * 0.1).astype(np.float32)
+    t = lambda a: torch.from_numpy(np.asarray(a)).to(dev, dt)  # noqa: E731
+    convs = {}
+    for k, (ci, co) in specs.items():
+        c = SparseConv3D(ci, co, 3).to(dev)
+        c.conv.weight = t(ws[k])
+        c.conv.bias = t(bs[k])
+        convs[k] = c
+    x = SparseTensor(t(x0), torch.from_numpy(coords).to(dev))
+    b_idx = x.coords[:, 0].long()
+    sc, sh, sw, sb = t(scale)[b_idx], t(shift)[b_idx], t(skip_w), t(skip_b)
+
+    def ln32(h):
+        return F.layer_norm(h.float(), (h.shape[-1],), None, None, 1e-6).to(h.dtype)
+
+    def run():
+        h = x.replace(F.silu(ln32(x.features)))
+        h = convs["c1"](h)
+        h = h.replace(ln32(h.features) * (1 + sc) + sh)
+        h = convs["c2"](h.replace(F.silu(h.features)))
+        h = h + (x.features @ sw.T + sb)
+        d = convs["c3"](sparse_downsample(h, 2))
+        u = convs["c4"](sparse_upsample(d, 2))
+        return convs["c5"](u)
+
+    def cpu_run(element: int):
+        c = per[element]
+        f = x0[coords[:, 0] == element]
+        conv = lambda a, k, nb: O.sparse_conv3d_fallback_literal(  # noqa: E731
+            a, nb, O.spconv_weight_to_kio(ws[k]), bs[k])
+        nbr = O.build_neighbor_map_dict(c, 3)
+        r = O.silu(O.layernorm32(f))
+        r = conv(r, "c1", nbr)
+        r = O.layernorm32(r) * (1 + scale[element]) + shift[element]
+        r = conv(O.silu(r), "c2", nbr)
+        r = r + (f @ skip_w.T + skip_b)
+        dc, inv = O.downsample_coords(c, 2)
+        r = O.downsample_features(r, inv, len(dc))
+        r = conv(r, "c3", O.build_neighbor_map_dict(dc, 3))
+        r = O.upsample_features(r, inv)
+        r = conv(r, "c4", nbr)
+        return conv(r, "c5", nbr)
+
+    return run, specs, x, cpu_run
+
+
+def secondary_block(args, dev, flush) -> dict:
+    """The other BASELINE configurations, device-timed on this GPU beside the headline, each with
+    its roofline fraction and the reference's algorithm timed on the host cores (a bounded
+    sample, stated): config 1 (fp32), config 3 (the fp16 I/O stack), config 4's two convs, and
+    a bounded part of config 5's sweep with the kernel-map time separate from the conv time.
+    The full sweep is ``--workload sweep``."""
+
+    import torch
+
+    from mlx_diffuser_b200 import _native as N
+    from mlx_diffuser_b200 import scenes
+    from oracle import sparse_oracle as O
+
+    out = {}
+    peaks = measured_peaks()
+    # ---- config 1: fp32, 64^3 shell, 128 -> 128 ----
+    coords = scenes.shell64(0)
+    ms, pairs, x, roof = conv_timing(args, dev, flush, coords, 128, 128, torch.float32, 21)
+    n = len(coords)
+    flops = 2.0 * 128 * 128 * pairs
+    ffma_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    achieved = flops / (ms * 1e-3) / 1e12
+    use_all_host_cores()
+    wk = O.spconv_weight_to_kio(scenes.conv_weight(128, 128, 3, 22))
+    feats = scenes.normal_features(n, 128, 21)
+    t0 = time.perf_counter()
+    cpu_step(coords, feats, wk, np.zeros(128, np.float32))
+    cpu_s = time.perf_counter() - t0
+    out["config1"] = {
+        "workload": "shell64_conv128to128_fp32", "voxels": n, "valid_pairs": pairs, "ms": ms,
+        "voxels_per_s": n / (ms * 1e-3),
+        "roofline": {"bound": "fp32", "kernel": conv_kernel_name(torch.float32, 128, 128),
+                     "achieved": achieved, "unit": "TFLOP/s", "peak": ffma_peak,
+                     "frac": achieved / ffma_peak,
+                     "peak_source": "148 SMs x 128 FP32 lanes x 2 x 1965 MHz (nominal FFMA)",
+                     "frac_of_roofline_time": roof["frac_of_roofline_time"]},
+        "cpu_baseline": {"value": n / cpu_s, "unit": "voxels/s", "cores": blas_threads(),
+                         "kind": "port", "sample": f"the whole scene ({n} voxels), one run"},
+    }
+    # ---- config 3: the fp16 I/O stack ----
+    dt = torch.float16
+    run, specs, x3, cpu_run = config3_stack(dev, dt)
+    run()
+    ms = _time_device(run, args.steps, args.warmup, flush)
+    n3 = x3.num_points
+    roof_ms = 0.0
+    nbr_f = x3.cache["neighbors_3_1_(1, 1, 1)"]
+    pairs_f = int((nbr_f >= 0).sum().item())
+    nbr_c = x3.cache["neighbors_3_1_(2, 2, 2)"]  # the coarse level's map (shared cache)
+    m = int(nbr_c.shape[0])
+    pairs_c = int((nbr_c >= 0).sum().item())
+    for k, (ci, co) in specs.items():
+        rows, p = (m, pairs_c) if k == "c3" else (n3, pairs_f)
+        roof_ms += conv_roofline(rows, ci, co, p, dt, 1.0)["roofline_ms"]
+    # element-wise passes (two LN32 + SiLU, skip add) and the two pools: one read + one write
+    roof_ms += 2.0 * n3 * (8 * 2 + 128 * 4) / (peaks["hbm_gbs"] * 1e9) * 1e3
+    roof_ms += 2.0 * (n3 * 128 + m * 128 + m * 1024 + n3 * 1024) / (peaks["hbm_gbs"] * 1e9) * 1e3
+    use_all_host_cores()
+    t0 = time.perf_counter()
+    cpu_run(0)
+    cpu_s = time.perf_counter() - t0
+    n0 = int((x3.coords[:, 0] == 0).sum().item())
+    out["config3"] = {
+        "workload": "slat_io_stack_shell64x2_fp16", "voxels": n3, "coarse_voxels": m, "ms": ms,
+        "voxels_per_s": n3 / (ms * 1e-3),
+        "stack": "resblock 8->128 (LN32, SiLU, 1x1 skip), downsample, conv 128->1024, "
+                 "upsample, conv 1024->128, conv 128->8",
+        "roofline": {"bound": "tensor+hbm", "roofline_ms": roof_ms,
+                     "frac_of_roofline_time": roof_ms / ms, "peak_source": peaks["source"]},
+        "cpu_baseline": {"value": n0 / cpu_s, "unit": "voxels/s", "cores": blas_threads(),
+                         "kind": "port",
+                         "sample": f"batch element 0 ({n0} voxels): dict maps + the fallback "
+                                   "and pooling of the reference, fp32"},
+    }
+    del x3, run
+    # ---- config 4: the 128^3 scene, convs 64 -> 64 and 64 -> 32 ----
+    coords = scenes.scene128(0)
+    n = len(coords)
+    convs4 = []
+    for cin, cout in ((64, 64), (64, 32)):
+        ms, pairs, _, roof = conv_timing(args, dev, flush, coords, cin, cout, torch.bfloat16, 11)
+        convs4.append({"conv": f"{cin}->{cout}", "ms": ms, "voxels_per_s": n / (ms * 1e-3),
+                       "valid_pairs": pairs, "kernel": conv_kernel_name(torch.bfloat16, cin, cout),
+                       "roofline": roof})
+    wk = O.spconv_weight_to_kio(scenes.conv_weight(64, 64, 3, 12))
+    out["config4"] = {
+        "workload": "scene128_conv64to64_conv64to32_bf16", "voxels": n, "convs": convs4,
+        "cpu_baseline": cpu_conv_sample(coords, scenes.normal_features(n, 64, 11), wk, 20000),
+    }
+    # ---- config 5: a bounded part of the sweep (map and conv timed separately) ----
+    cells = []
+    for layout, grid, occ in (("uniform", 64, 0.08), ("shell", 64, 0.08), ("uniform", 128, 0.02),
+                              ("shell", 128, 0.02), ("uniform", 128, 0.30)):
+        gen = scenes.uniform if layout == "uniform" else scenes.shell_fraction
+        coords = scenes.batched([gen(grid, occ, 700 + b) for b in range(16)])
+        ms_map, roof_map = map_timing(args, dev, flush, coords)
+        for ch in (32, 128, 1024):
+            n = len(coords)
+            feats = torch.randn((n, ch), device=dev, dtype=torch.bfloat16)
+            ms, pairs, _, roof = conv_timing(args, dev, flush, coords, ch, ch, torch.bfloat16, 13,
+                                             feats=feats)
+            cells.append({"cell": f"{layout}{grid}x16_{occ:g}_c{ch}_bf16", "voxels": n,
+                          "valid_pairs": pairs, "kmap_ms": ms_map,
+                          "kmap_roofline_frac": roof_map["frac"], "conv_ms": ms,
+                          "conv_voxels_per_s": n / (ms * 1e-3),
+                          "kernel": conv_kernel_name(torch.bfloat16, ch, ch),
+                          "conv_roofline": roof})
+            del feats
+        torch.cuda.empty_cache()
+    coords = scenes.uniform(128, 0.02, 700)
+    wk = O.spconv_weight_to_kio(scenes.conv_weight(128, 128, 3, 14))
+    out["config5"] = {
+        "workload": "occupancy/width sweep, batch 16 (bounded: 5 cells x 3 widths)",
+        "cells": cells,
+        "cpu_baseline": dict(cpu_conv_sample(coords, scenes.normal_features(len(coords), 128, 13),
+                                             wk, 20000),
+                             sample="one element (uniform 128^3 at 2%), width 128: dict of all "
+                                    f"{len(coords)} rows + lookups and fallback for 20000 rows"),
+    }
+    N.check_device_status(dev)
+    return out
+
+
+def conv_kernel_name(dtype, cin, cout) -> str:
+    """The kernel ``sv_conv3d_forward`` picks for this shape (AUTO)."""
+
+    import torch
+
+    if dtype in (torch.float16, torch.bfloat16) and cin % 32 == 0 and cout % 32 == 0:
+        bn = 256 if cout % 256 == 0 else 128 if cout % 128 == 0 else 64 if cout % 64 == 0 else 32
+        bk = 64 if cin % 64 == 0 else 32
+        return f"conv_tc_kernel<{bn}, {bk}>"
+    if dtype == torch.float32 and cin % 4 == 0 and cout % 4 == 0:
+        return "conv_f32_kernel"
+    return "conv_simt_kernel"
+
+
+def link_ceiling(coords_h, feats_h, out_h, out_d, c_d, f_d, dev, reps: int = 10) -> dict:
+    """The host link's ceiling for the e2e step's traffic, measured in the same run: the step's
+    H2D (coordinates + features, pinned) and D2H (the output, pinned) copied concurrently on two
+    streams, ``reps`` times, on every rank at once (the caller synchronises the ranks first).
+    Returns GB/s of H2D + D2H bytes over the time of the slower stream."""
+
+    import torch
+
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    start = torch.cuda.Event(enable_timing=True)
+    e_in, e_out = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    start.record()
+    s_in.wait_event(start)
+    s_out.wait_event(start)
+    with torch.cuda.stream(s_in):
+        for _ in range(reps):
+            c_d.copy_(coords_h, non_blocking=True)
+            f_d.copy_(feats_h, non_blocking=True)
+        e_in.record(s_in)
+    with torch.cuda.stream(s_out):
+        for _ in range(reps):
+            out_h.copy_(out_d, non_blocking=True)
+        e_out.record(s_out)
+    torch.cuda.synchronize(dev)
+    ms = max(start.elapsed_time(e_in), start.elapsed_time(e_out))
+    h2d = coords_h.numel() * coords_h.element_size() + feats_h.numel() * feats_h.element_size()
+    d2h = out_h.numel() * out_h.element_size()
+    return {"gbs": reps * (h2d + d2h) / (ms * 1e-3) / 1e9,
+            "h2d_gbs": reps * h2d / (start.elapsed_time(e_in) * 1e-3) / 1e9,
+            "d2h_gbs": reps * d2h / (start.elapsed_time(e_out) * 1e-3) / 1e9}
+
+
 def run_workload(args) -> None:
     import torch
 
     from mlx_diffuser_b200 import _native as N
     from mlx_diffuser_b200 import scenes
     from mlx_diffuser_b200.layers.sparse import (
-        SparseConv3D,
         SparseTensor,
-        build_neighbor_map,
         sparse_downsample,
         sparse_upsample,
     )
@@ -628,41 +1016,10 @@ def run_workload(args) -> None:
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def conv_case(coords, cin, cout, dtype, seed):
-        n = len(coords)
-        c = torch.from_numpy(coords).to(dev)
-        f = torch.from_numpy(scenes.normal_features(n, cin, seed)).to(dev, dtype)
-        conv = SparseConv3D(cin, cout, 3).to(dev)
-        conv.conv.weight = torch.from_numpy(scenes.conv_weight(cout, cin, 3, seed + 1)).to(dev, dtype)
-        conv.conv.bias = torch.zeros(cout, device=dev, dtype=dtype)
-        x = SparseTensor(f, c, int(coords[:, 0].max()) + 1, None)
-        conv(x)  # builds and caches the map and schedule
-        nbr = x.cache["neighbors_3_1_(1, 1, 1)"]
-        pairs = int((nbr >= 0).sum().item())
-        ms = _time_device(lambda: conv(x), args.steps, args.warmup, flush)
-        flops = 2.0 * cin * cout * pairs
-        dsz = torch.finfo(dtype).bits // 8
-        bytes_ = dsz * n * (cin + cout) + dsz * 27 * cin * cout + 4 * 27 * n
-        peaks = measured_peaks()
-        t_tensor = flops / (peaks["bf16_tflops"] * 1e12)
-        t_hbm = bytes_ / (peaks["hbm_gbs"] * 1e9)
-        bound = "tensor" if t_tensor >= t_hbm else "hbm"
-        roof = (
-            {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
-             "unit": "TFLOP/s"}
-            if bound == "tensor"
-            else {"bound": "hbm", "achieved": bytes_ / (ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
-                  "unit": "GB/s"}
-        )
-        roof["frac"] = roof["achieved"] / roof["peak"]
-        roof["roofline_ms"] = max(t_tensor, t_hbm) * 1e3
-        roof["frac_of_roofline_time"] = roof["roofline_ms"] / ms
-        return ms, pairs, x, roof
+        return conv_timing(args, dev, flush, coords, cin, cout, dtype, seed)
 
     def map_case(coords):
-        c = torch.from_numpy(coords).to(dev)
-        n = len(coords)
-        ms = _time_device(lambda: build_neighbor_map(c, 3), args.steps, args.warmup, flush)
-        return ms, _hbm_roofline(16.0 * n + 4.0 * 27 * n, ms, "kmap_insert + kmap_probe")
+        return map_timing(args, dev, flush, coords)
 
     lines = []
     if args.workload == "kmap":
@@ -746,6 +1103,8 @@ def run_workload(args) -> None:
                             "groups": groups},
                            _hbm_roofline(16.0 * n + 4.0 * n + 4.0 * (groups + 1), ms,
                                          "window grouping (key sort + first-row sort)")))
+    elif args.workload == "hbm":
+        lines.extend(hbm_lines(args, dev, flush))
     elif args.workload == "resblock":
         lines.extend(resblock_lines(args, dev, flush))
     elif args.workload == "backward":
@@ -777,6 +1136,67 @@ def run_workload(args) -> None:
     for line in lines:
         print(json.dumps(line), flush=True)
     N.check_device_status(dev)
+
+
+def hbm_lines(args, dev, flush) -> list:
+    """The HBM-bound kernels, each timed alone (CUDA events, L2 flushed before every run) on the
+    inputs their ncu summary describes: the kernel map and the pooling of 4 x 128^3 scenes at 8%
+    uniform occupancy (128 bf16 channels), the fused row norm + SiLU on those rows at 1024
+    channels, subdivision of the pooled tensor and occupancy -> coordinates of 16 x 64^3 fp32
+    logits. One line per operation with its algorithmic bytes."""
+
+    import torch
+
+    from mlx_diffuser_b200 import scenes
+    from mlx_diffuser_b200.kernels.norm import row_norm
+    from mlx_diffuser_b200.layers.sparse import (
+        SparseTensor,
+        build_neighbor_map,
+        occupied_coordinates,
+        sparse_downsample,
+        sparse_subdivide,
+        sparse_upsample,
+    )
+
+    coords_np = scenes.batched([scenes.uniform(128, 0.08, 500 + b) for b in range(4)])
+    n = len(coords_np)
+    coords = torch.from_numpy(coords_np).to(dev)
+    feats = torch.from_numpy(scenes.normal_features(n, 128, 3)).to(dev, torch.bfloat16)
+    x = SparseTensor(feats, coords)
+    down = sparse_downsample(x, 2)
+    m = down.num_points
+    wide = torch.randn((n, 1024), device=dev, dtype=torch.bfloat16)
+    rng = np.random.default_rng(3)
+    logits = torch.from_numpy(rng.standard_normal((16, 64, 64, 64)).astype(np.float32) - 1.6)
+    logits = logits.to(dev)
+    occ = occupied_coordinates(logits, 0.0).shape[0]
+
+    def fresh_down():
+        x.cache.clear()
+        return sparse_downsample(x, 2)
+
+    cases = [
+        ("kernel-map build", "kmap_insert_kernel + kmap_probe_kernel",
+         lambda: build_neighbor_map(coords, 3), 16.0 * n + 4.0 * 27 * n, n),
+        ("sparse_downsample", "pool (coords sort + segment mean)", fresh_down,
+         16.0 * n + 16.0 * m + 4.0 * n + 2.0 * 128 * (n + m), n),
+        ("sparse_upsample", "gather_rows_kernel", lambda: sparse_upsample(down, 2),
+         4.0 * n + 2.0 * 128 * (m + n), n),
+        ("row norm + SiLU", "rownorm_vec_kernel", lambda: row_norm(wide, silu=True),
+         2.0 * 2 * 1024 * n, n),
+        ("sparse_subdivide", "subdivide_coords_kernel + expand_rows_kernel",
+         lambda: sparse_subdivide(down), 16.0 * m + 256.0 * m + 8 * (16.0 * m + 256.0 * m), m),
+        ("occupancy", "occ_count_kernel + occ_emit_kernel",
+         lambda: occupied_coordinates(logits, 0.0), 4.0 * logits.numel() + 16.0 * occ,
+         logits.numel()),
+    ]
+    lines = []
+    for name, kernel, fn, nbytes, units in cases:
+        ms = _time_device(fn, args.steps, args.warmup, flush)
+        lines.append(_line(f"{name} rows/s", units / (ms * 1e-3), "rows/s", ms, args,
+                           {"workload": f"hbm_uniform128x4_8pct: {name}", "rows": units},
+                           _hbm_roofline(nbytes, ms, kernel)))
+    return lines
 
 
 def resblock_lines(args, dev, flush) -> list:
@@ -958,12 +1378,19 @@ def backward_lines(args, dev, flush) -> list:
     ]
 
 
-def run_halo(args) -> None:
-    """One 128^3 scene (237k voxels) split over the ranks by Morton range. A step is what two
-    stacked ``SparseConv3D`` layers (64->64, 64->32, bf16) need on a partitioned scene: halo
-    exchange of the layer's input rows (NCCL send/recv), then the local tensor-core conv whose
-    output buffer is the next layer's local buffer. The plan and the local maps are built once,
-    like the reference's cached neighbour map. Strong scaling: total work is fixed."""
+def halo_measure(args, world: int, rank: int, local_rank: int, dev, sample_clocks=False) -> dict:
+    """Config 4's single scene (the 237k-voxel 128^3 union of six shells) split over the ranks
+    by Morton range. A step is what two stacked ``SparseConv3D`` layers (64->64, 64->32, bf16)
+    need on a partitioned scene: each layer's halo rows are pushed into the peers' buffers over
+    NVLink by the library's kernel while the interior rows are convolved, all in one tcgen05
+    launch per layer (at one rank: the two convolutions). The NCCL point-to-point variant
+    (exchange, then conv) is timed beside it. The plan and the local maps are built once, like
+    the reference's cached neighbour map. Strong scaling: total work is fixed.
+
+    Parity, checked on the box after timing: every rank compares its own output rows (layer 2)
+    bit for bit with the single-GPU convolution of the whole scene, run on its own GPU, and
+    rank 0 compares that whole-scene result with the fp32 oracle chain (max relative error
+    1e-2). Collective calls are the same on every rank. Returns the measurements (all ranks)."""
 
     import torch
     import torch.distributed as dist
@@ -980,21 +1407,13 @@ def run_halo(args) -> None:
     from mlx_diffuser_b200.kernels.sparse import conv3d_forward
     from mlx_diffuser_b200.layers.sparse import build_neighbor_map, conv_row_order
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     coords_np = scenes.scene128(0)
     n = len(coords_np)
     coords = torch.from_numpy(coords_np).to(dev)
     nbr = build_neighbor_map(coords, 3)
     plan = HaloPlan.build(coords, nbr, rank, world)
     lnbr = plan.local_nbr.to(dev)
+    plan.local_nbr = lnbr
     row_order, tile_order = conv_row_order(lnbr)
     dt = torch.bfloat16
     w1 = torch.from_numpy(scenes.conv_weight(64, 64, 3, 41)).to(dev, dt).contiguous()
@@ -1024,10 +1443,11 @@ def run_halo(args) -> None:
     halo_h = PeerHalo(plan, h_local) if world > 1 else None
 
     def step():
-        # each layer: push this rank's rows into the peers' halo blocks over NVLink, convolve
-        # the interior rows meanwhile, wait for the peers' rows, convolve the boundary rows
         if world == 1:
-            nccl_overlap_step()
+            conv3d_forward(x_local, lnbr, w1, N.SV_WEIGHT_OKI, b1, 64, row_order=row_order,
+                           tile_order=tile_order, out=h_local)
+            conv3d_forward(h_local, lnbr, w2, N.SV_WEIGHT_OKI, b2, 32, row_order=row_order,
+                           tile_order=tile_order, out=y_local)
             return
         halo_conv_p2p(halo_x, w1, b1, out=h_local)
         halo_conv_p2p(halo_h, w2, b2, out=y_local)
@@ -1037,14 +1457,14 @@ def run_halo(args) -> None:
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize()
 
-    def timed(fn, sample_clocks=False):
+    def timed(fn, with_clocks=False):
         for _ in range(max(args.warmup, 1)):
             fn()
         barrier()
         N.check_device_status(dev)
         events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(args.steps)]
-        sampler = ClockSampler(local_rank) if sample_clocks else None
+        sampler = ClockSampler(local_rank) if with_clocks else None
         barrier()
         if sampler:
             sampler.start()
@@ -1060,52 +1480,108 @@ def run_halo(args) -> None:
     serial_ms, _ = timed(serial_step)
     y_serial = y_local[: plan.num_own].clone()
     nccl_overlap_ms, _ = timed(nccl_overlap_step)
-    assert torch.equal(y_local[: plan.num_own], y_serial), "overlapped halo conv differs"
-    overlap_ms, clocks = timed(step, sample_clocks=True)
-    assert torch.equal(y_local[: plan.num_own], y_serial), "peer-memory halo conv differs"
-    ms = torch.tensor([overlap_ms, serial_ms, nccl_overlap_ms], dtype=torch.float64, device=dev)
-    halo = torch.tensor([float(plan.halo.numel())], dtype=torch.float64, device=dev)
+    same_overlap = torch.equal(y_local[: plan.num_own], y_serial)
+    step_ms, clocks = timed(step, with_clocks=sample_clocks)
+    same_p2p = torch.equal(y_local[: plan.num_own], y_serial)
+    N.check_device_status(dev)
+
+    # ---- parity: own rows vs the whole scene on this GPU; rank 0: whole scene vs the oracle
+    full_order, full_tiles = conv_row_order(nbr)
+    h_full = conv3d_forward(feats, nbr, w1, N.SV_WEIGHT_OKI, b1, 64, row_order=full_order,
+                            tile_order=full_tiles)
+    y_full = conv3d_forward(h_full, nbr, w2, N.SV_WEIGHT_OKI, b2, 32, row_order=full_order,
+                            tile_order=full_tiles)
+    torch.cuda.synchronize()
+    rank_ok = bool(same_overlap and same_p2p and
+                   torch.equal(y_local[: plan.num_own], y_full[plan.own]))
+    oracle_err = None
+    if rank == 0:
+        from oracle import sparse_oracle as O
+
+        nb = nbr.cpu().numpy()
+        f32 = feats.float().cpu().numpy()
+        r1 = O.sparse_conv3d(f32, nb, O.spconv_weight_to_kio(w1.float().cpu().numpy()),
+                             np.zeros(64, np.float32))
+        r2 = O.sparse_conv3d(r1, nb, O.spconv_weight_to_kio(w2.float().cpu().numpy()),
+                             np.zeros(32, np.float32))
+        got = y_full.float().cpu().numpy()
+        oracle_err = float(np.abs(got - r2).max() / np.abs(r2).max())
+        rank_ok = rank_ok and oracle_err <= 1e-2
+
+    ms = torch.tensor([step_ms, serial_ms, nccl_overlap_ms], dtype=torch.float64, device=dev)
+    sums = torch.tensor([float(plan.halo.numel()), 0.0 if rank_ok else 1.0],
+                        dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        dist.all_reduce(halo)
-    ms_v, serial_v, nccl_ov_v = (float(v) for v in ms.cpu())
-    halo_v = float(halo.item())
-    if rank == 0:
-        pairs = int((nbr >= 0).sum().item())
-        print(json.dumps({
-            "metric": "sparse conv3d active-voxels/s (2 stacked layers, one partitioned scene)",
-            "value": n / (ms_v * 1e-3),
-            "unit": "voxels/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": ms_v,
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic",
-            "config": {
-                "workload": "scene128_halo_conv64to64to32_bf16",
-                "voxels": n,
-                "valid_pairs": pairs,
-                "halo_rows_total": int(halo_v),
-                "halo_fraction": halo_v / n,
-                "parallelism": f"morton-range x{world}",
-                "exchange": "rows pushed into the peers' halo blocks over NVLink by the "
-                            "library's kernel (CUDA IPC), flags with system-scope release / "
-                            "acquire; interior rows convolved meanwhile",
-                "nccl_serial_ms_per_step": serial_v,
-                "nccl_overlapped_ms_per_step": nccl_ov_v,
-                "l2": "flushed between steps (256 MiB write outside the timed events)",
-            },
-            "clocks": clocks,
-        }), flush=True)
+        dist.all_reduce(sums)
+    step_v, serial_v, nccl_ov_v = (float(v) for v in ms.cpu())
+    halo_rows, bad_ranks = (float(v) for v in sums.cpu())
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize()
         halo_x.close()
         halo_h.close()
+        dist.barrier(device_ids=[local_rank])
+    pairs = int((nbr >= 0).sum().item())
+    return {
+        "workload": "scene128_halo_conv64to64to32_bf16",
+        "ms_per_step": step_v,
+        "voxels_per_s": n / (step_v * 1e-3),
+        "voxels": n,
+        "valid_pairs": pairs,
+        "halo_rows_total": int(halo_rows),
+        "halo_fraction": halo_rows / n,
+        "parallelism": f"morton-range x{world}",
+        "exchange": ("none (one GPU)" if world == 1 else
+                     "rows pushed into the peers' halo blocks over NVLink by the library's "
+                     "kernel (CUDA IPC), flags with system-scope release / acquire; one tcgen05 "
+                     "launch per layer, the boundary tiles wait in the kernel"),
+        "nccl_serial_ms_per_step": serial_v,
+        "nccl_overlapped_ms_per_step": nccl_ov_v,
+        "parity_ok": bad_ranks == 0,
+        "parity": "every rank's own rows bit-exact to the single-GPU conv of the whole scene; "
+                  "rank 0: whole scene vs the fp32 oracle chain, max relative error "
+                  f"{oracle_err if oracle_err is not None else float('nan'):.2e} (<= 1e-2)",
+        "scaling": "strong",
+        "l2": "flushed between steps (256 MiB write outside the timed events)",
+        "clocks": clocks,
+    }
+
+
+def run_halo(args) -> None:
+    """``--workload halo``: the halo measurement alone, one JSON line (see halo_measure)."""
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    h = halo_measure(args, world, rank, local_rank, dev, sample_clocks=True)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "sparse conv3d active-voxels/s (2 stacked layers, one partitioned scene)",
+            "value": h["voxels_per_s"],
+            "unit": "voxels/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": h["ms_per_step"],
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {k: v for k, v in h.items() if k not in ("clocks",)},
+            "clocks": h["clocks"],
+        }), flush=True)
+    if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
 

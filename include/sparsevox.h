@@ -99,8 +99,10 @@ SV_API int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t kernel[
  * the process exits) instead of caller workspace; nothing is allocated.
  * Limits and rules:
  *  - n <= SV_KMAP_STATIC_MAX_ROWS, otherwise SV_ERR_UNSUPPORTED (with a message) and no work;
- *  - the first call on a device looks up the array's device address (cudaGetSymbolAddress), so
- *    make that first call before any stream capture;
+ *  - a call outside stream capture looks up the array's device address (cudaGetSymbolAddress),
+ *    so it stays valid after the caller resets the device; a call on a capturing stream reuses
+ *    the address found by that device's last call outside capture, so make one call on the
+ *    device before capturing (and again after a reset);
  *  - all calls on a device share the one table: calls that overlap on the GPU race. Each call
  *    clears the slots it uses before inserting, so back-to-back calls are independent. */
 #define SV_KMAP_STATIC_MAX_ROWS 524288

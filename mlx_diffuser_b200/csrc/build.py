@@ -14,6 +14,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
@@ -61,11 +62,16 @@ def build(force: bool = False, verbose: bool = False) -> str:
     ]
     if verbose:
         common.append("-Xptxas=-v")
-    objs = []
-    for src in SOURCES:
-        obj = os.path.join(obj_dir, src.replace(".cu", ".o"))
+    objs = [os.path.join(obj_dir, src.replace(".cu", ".o")) for src in SOURCES]
+
+    def compile_one(src_obj):
+        src, obj = src_obj
         subprocess.run([nvcc(), *common, "-c", os.path.join(HERE, src), "-o", obj], check=True)
-        objs.append(obj)
+
+    # one nvcc per translation unit, in parallel (each is single-threaded)
+    workers = max(1, min(len(SOURCES), os.cpu_count() or 1))
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        list(pool.map(compile_one, zip(SOURCES, objs)))
     tmp = LIB + ".tmp"
     subprocess.run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs], check=True)
     os.replace(tmp, LIB)

@@ -428,17 +428,25 @@ std::mutex g_static_table_mu;
 int32_t* g_static_table_addr[256] = {};
 
 // Device address of sv_kmap_static_table on the current device. In host code the array's name
-// only stands in for the symbol, so the address is looked up once per device (with that device
-// current) and reused.
-int static_table_address(int32_t** out) {
+// only stands in for the symbol, so the address is looked up with the device current. A call
+// outside stream capture looks it up afresh (the module, and so the array's address, changes
+// when the caller resets the device or recreates its primary context) and remembers it; a call
+// made while `stream` is capturing cannot look it up and uses the remembered one, which a call
+// on that device before the capture must have stored.
+int static_table_address(cudaStream_t stream, int32_t** out) {
   int dev = 0;
   SV_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 256) SV_FAIL(SV_ERR_UNSUPPORTED, "device index above 255");
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  SV_CUDA_TRY(cudaStreamIsCapturing(stream, &capture));
   std::lock_guard<std::mutex> lock(g_static_table_mu);
-  if (g_static_table_addr[dev] == nullptr) {
+  if (capture == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     SV_CUDA_TRY(cudaGetSymbolAddress(&p, sv_kmap_static_table));
     g_static_table_addr[dev] = static_cast<int32_t*>(p);
+  } else if (g_static_table_addr[dev] == nullptr) {
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT,
+            "sv_kmap_build_static: the first call on a device must come before stream capture");
   }
   *out = g_static_table_addr[dev];
   return SV_OK;
@@ -456,7 +464,7 @@ extern "C" int sv_kmap_build_static(const int32_t* coords, int64_t n, const int3
   const int64_t slots = sv_kmap_table_slots(n);  // <= 2 * SV_KMAP_STATIC_MAX_ROWS
   int32_t* table = nullptr;
   if (n > 0) {
-    const int rc = static_table_address(&table);
+    const int rc = static_table_address(to_stream(stream), &table);
     if (rc != SV_OK) return rc;
   }
   // sv_kmap_build clears the `slots` words it uses to -1 before inserting, so nothing of an

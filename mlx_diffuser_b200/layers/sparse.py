@@ -43,9 +43,10 @@ def _triple(value, what: str) -> tuple[int, int, int]:
 
 @dataclasses.dataclass
 class SparseTensor:
-    """Minimal sparse tensor shared by TRELLIS flow and representation decoders.
+    """Device-resident voxel set: one feature row per occupied coordinate, on CUDA tensors.
 
-    ``coords`` are int32 rows ``(batch, x, y, z)``; ``features`` hold one row per coordinate.
+    The fields, defaults and validation follow the reference's container so that callers of
+    its sparse layers can pass this one unchanged. ``coords`` are int32 rows ``(batch, x, y, z)``; ``features`` hold one row per coordinate.
     ``cache`` is shared by every tensor derived through :meth:`replace` and holds the
     neighbour maps (``neighbors_{k}_{dilation}_{scale}``) and down/upsample inverses
     (``upsample_{factor}_{scale}``), as in ``src/mlx_diffuser/layers/sparse.py:23-143``.

@@ -8,6 +8,7 @@ the CUDA path, the CPU oracle and the benchmark see identical inputs.
   latent is a surface layer of this kind (about 13.5k voxels at 64^3 for a real object).
 * :func:`shell_union` -- the union of several such shells at random centres.
 * :func:`uniform` -- independent uniform occupancy at a given fraction.
+* :func:`shell_fraction` -- a noisy shell holding a given fraction of the grid's cells.
 
 Coordinates are int32 rows ``(batch, x, y, z)`` in lexicographic order (the order
 ``np.argwhere`` gives the occupancy grid, as the reference's structure decoder does).
@@ -78,6 +79,28 @@ def uniform(grid: int, fraction: float, seed: int, batch: int = 0) -> np.ndarray
     rng = np.random.default_rng(seed)
     occ = rng.random((grid, grid, grid)) < fraction
     return _with_batch(np.argwhere(occ), batch)
+
+
+def shell_fraction(grid: int, fraction: float, seed: int, batch: int = 0) -> np.ndarray:
+    """A noisy sphere shell holding ``round(fraction * grid^3)`` voxels: the surface-shell
+    layout of the occupancy sweep.
+
+    The radius is the one at which a 2-voxel-thick shell has the target count, capped at
+    0.36 * grid (so the shell stays inside the box); the shell is then the target number of
+    cells nearest the perturbed sphere (it thickens instead of growing once the radius is
+    capped, e.g. about 12 voxels thick at 30% of 64^3)."""
+
+    target = int(round(fraction * grid**3))
+    rng = np.random.default_rng(seed)
+    radius = min(np.sqrt(target / (8.0 * np.pi)), 0.36 * grid)
+    c = (grid - 1) / 2.0
+    d = _perturbed_distance(grid, (c, c, c), radius, 0.08 * radius, rng).ravel()
+    if target <= 0:
+        return _with_batch(np.zeros((0, 3), np.int64), batch)
+    # the `target` nearest cells (ties broken by cell index), in argwhere (row-major) order
+    keep = np.sort(np.argsort(d, kind="stable")[:target])
+    xyz = np.stack(np.unravel_index(keep, (grid, grid, grid)), axis=1)
+    return _with_batch(xyz, batch)
 
 
 def batched(scenes: list[np.ndarray]) -> np.ndarray:

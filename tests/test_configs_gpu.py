@@ -4,8 +4,9 @@
 * config 3: SLat-flow-style I/O stack in fp16, batch 2 (ResBlock 8 -> 128 with a 1x1 skip,
   downsample, conv 128 -> 1024, upsample, convs 1024 -> 128 -> 8), max relative error 1e-2;
 * config 4: 128^3 union of six shells (~237k voxels), convs 64 -> 64 -> 32 in bf16;
-* config 5: uniform occupancy 0.5 / 2 / 8 / 30 % on 64^3 and 128^3, batch 16, widths
-  32 / 128 / 512 / 1024 in bf16 (kernel maps bit-exact; convs on sampled rows).
+* config 5: uniform and surface-shell occupancy 0.5 / 2 / 8 / 30 % on 64^3 and 128^3, batch 16,
+  widths 32 / 128 / 512 / 1024 in bf16 (kernel maps bit-exact; convs on sampled rows against the
+  oracle and on every row through random projections).
 
 For the fp16/bf16 cases the reference is computed in fp32 from the same rounded inputs and
 weights; "max relative error" is max|out - ref| / max|ref|.
@@ -27,6 +28,7 @@ from mlx_diffuser_b200.layers.sparse import (
     sparse_upsample,
 )
 from oracle import sparse_oracle as O
+from tests.fullsize import device_features, oracle_rows, projection_error
 
 pytestmark = pytest.mark.gpu
 
@@ -153,6 +155,10 @@ def test_config3_slat_io_stack_fp16():
 
 
 def test_config4_scene128_convs_64_64_32_bf16():
+    """Both layers against the fp32 oracle: layer 1 on its own, and the two-layer chain against
+    the oracle's fp32 chain from the original inputs (the GPU rounds the 64-channel intermediate
+    to bf16; the oracle does not), so the two-layer error growth is measured too."""
+
     dtype = torch.bfloat16
     coords = scenes.scene128(0)
     f = _rounded(scenes.normal_features(len(coords), 64, seed=40), dtype)
@@ -167,40 +173,57 @@ def test_config4_scene128_convs_64_64_32_bf16():
     assert np.array_equal(x.cache["neighbors_3_1_(1, 1, 1)"].cpu().numpy(), nbr)
     r1 = O.sparse_conv3d(f, nbr, O.spconv_weight_to_kio(w1), z64)
     assert max_rel_err(h.features.float().cpu().numpy(), r1) <= 1e-2
-    # second conv against the reference applied to the GPU's (bf16) first-layer output
-    h_np = h.features.float().cpu().numpy()
-    r2 = O.sparse_conv3d(h_np, nbr, O.spconv_weight_to_kio(w2), z32)
+    # the chain: layer 2 of the oracle consumes the oracle's own fp32 layer-1 output
+    r2 = O.sparse_conv3d(r1, nbr, O.spconv_weight_to_kio(w2), z32)
     assert max_rel_err(y.features.float().cpu().numpy(), r2) <= 1e-2
 
 
 # ---- config 5 -------------------------------------------------------------------------------
 
+CONFIG5_WIDTHS = (32, 128, 512, 1024)
+SAMPLED_ROWS = 1024
 
+
+def config5_coords(layout: str, grid: int, occupancy: float) -> np.ndarray:
+    """16 independently seeded elements of one sweep cell."""
+
+    if layout == "uniform":
+        return scenes.batched([scenes.uniform(grid, occupancy, 900 + b) for b in range(16)])
+    return scenes.batched([scenes.shell_fraction(grid, occupancy, 950 + b) for b in range(16)])
+
+
+@pytest.mark.parametrize("layout", ["uniform", "shell"])
 @pytest.mark.parametrize("grid", [64, 128])
 @pytest.mark.parametrize("occupancy", [0.005, 0.02, 0.08, 0.30])
-def test_config5_uniform_occupancy_maps_and_convs(grid, occupancy):
+def test_config5_sweep_maps_and_convs(layout, grid, occupancy):
+    """One cell of the occupancy x width sweep, batch 16, every width (up to 10M rows x 1024
+    channels). The kernel map is compared bit-exactly with the oracle's. Each conv is compared
+    with the fp32 oracle on 1024 sampled rows and, for every row, through random projections of
+    the output channels (tests/fullsize.py), both as max relative error <= 1e-2."""
+
     dtype = torch.bfloat16
-    coords = scenes.batched([scenes.uniform(grid, occupancy, 900 + b) for b in range(16)])
+    coords = config5_coords(layout, grid, occupancy)
     c = torch.from_numpy(coords).to(DEV)
     nbr_gpu = build_neighbor_map(c, 3)
     nbr = O.build_neighbor_map(coords, 3)
     assert np.array_equal(nbr_gpu.cpu().numpy(), nbr)
-    rng = np.random.default_rng(grid + int(occupancy * 1000))
-    rows = rng.choice(len(coords), min(256, len(coords)), replace=False)
-    for ch in (32, 128, 512, 1024):
-        if len(coords) * ch > 1_500_000_000:
-            continue  # the largest widths at the densest 128^3 case exceed the test's budget
-        f = _rounded(scenes.normal_features(len(coords), ch, seed=ch), dtype)
+    del nbr
+    n = len(coords)
+    rng = np.random.default_rng(grid + int(occupancy * 1000) + (7 if layout == "shell" else 0))
+    rows = rng.choice(n, min(SAMPLED_ROWS, n), replace=False)
+    for ch in CONFIG5_WIDTHS:
+        f = device_features(n, ch, seed=ch, dtype=dtype, device=DEV)
         w = _rounded(scenes.conv_weight(ch, ch, 3, ch + 1), dtype)
         b = np.zeros(ch, np.float32)
-        x = SparseTensor(torch.from_numpy(f).to(DEV, dtype), c)
+        x = SparseTensor(f, c)
         x.cache["neighbors_3_1_(1, 1, 1)"] = nbr_gpu
-        out = _conv(ch, ch, w, b, dtype)(x).features[torch.from_numpy(rows).to(DEV)]
+        out = _conv(ch, ch, w, b, dtype)(x).features
+        N.check_device_status(DEV)
         wk = O.spconv_weight_to_kio(w)
-        ref = np.zeros((len(rows), ch), np.float32)
-        for k in range(27):
-            idx = nbr[rows, k]
-            ok = idx >= 0
-            ref[ok] += f[idx[ok]] @ wk[k]
-        assert max_rel_err(out.float().cpu().numpy(), ref) <= 1e-2, ch
-    N.check_device_status(DEV)
+        ref = oracle_rows(f, nbr_gpu, rows, wk, b)
+        got = out[torch.from_numpy(rows).to(DEV)].float().cpu().numpy()
+        assert max_rel_err(got, ref) <= 1e-2, (ch, "sampled rows")
+        err = projection_error(out, f, nbr_gpu, torch.from_numpy(wk), None)
+        assert err <= 1e-2, (ch, "all rows", err)
+        del f, x, out
+    torch.cuda.empty_cache()

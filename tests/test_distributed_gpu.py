@@ -1,5 +1,11 @@
-"""Morton-range partition of one scene over two GPUs: NCCL point-to-point halo exchange plus the
-tensor-core conv on each rank must reproduce the single-GPU conv of the whole scene."""
+"""Morton-range partition of one scene.
+
+* On one GPU: every rank's share of a partitioned scene (2, 4 and 8 ranks) is convolved in turn
+  on the local buffer the halo exchange produces -- by the local tensor-core conv and by the
+  single-launch halo conv whose in-kernel wait finds its flags already raised -- and the union of
+  the ranks' own rows is compared with the fp32 oracle of the whole scene.
+* On two GPUs: NCCL point-to-point and NVLink peer-memory exchanges plus the tensor-core conv on
+  each rank must reproduce the single-GPU conv of the whole scene, and the fp32 oracle."""
 
 from __future__ import annotations
 
@@ -60,6 +66,15 @@ def _worker(rank: int, world: int, port: int, errors):
         ref = full[plan.own]
         err = (out_own.float() - ref.float()).abs().max() / ref.float().abs().max()
         assert float(err) <= 1e-6, float(err)
+        # and the fp32 oracle on this rank's rows
+        from oracle import sparse_oracle as O
+
+        own_np = plan.own.cpu().numpy()
+        f32 = feats.float().cpu().numpy()
+        oracle = O.sparse_conv3d(f32, nbr.cpu().numpy(), O.spconv_weight_to_kio(
+            w.float().cpu().numpy()), b.float().cpu().numpy())[own_np]
+        got = out_own.float().cpu().numpy()
+        assert float(np.abs(got - oracle).max() / np.abs(oracle).max()) <= 1e-2
         # the overlapped variant: interior rows while the exchange is in flight, then boundary
         local2 = torch.zeros_like(local)
         local2[: plan.num_own] = feats[plan.own]
@@ -84,6 +99,65 @@ def _worker(rank: int, world: int, port: int, errors):
     except Exception as e:  # pragma: no cover - reported through the queue
         errors.put(f"rank {rank}: {e!r}")
         raise
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_partitioned_scene_on_one_gpu_matches_oracle(world):
+    """Each rank of a ``world``-way Morton partition, run one after another on one GPU: the local
+    buffer is filled as the exchange would fill it (own rows, then the halo rows by owner), then
+    convolved by the local tcgen05 conv and by the single-launch halo conv (its flags raised
+    beforehand, so the in-kernel wait passes at once). The ranks' own rows together must equal
+    the fp32 oracle of the whole scene (max relative error 1e-2) and each other (bit-exact)."""
+
+    import ctypes
+
+    from mlx_diffuser_b200 import _native as N
+    from mlx_diffuser_b200 import scenes
+    from mlx_diffuser_b200.distributed import HaloPlan, _fused_schedule, _subset_schedule
+    from mlx_diffuser_b200.kernels.sparse import conv3d_forward, conv3d_forward_halo
+    from mlx_diffuser_b200.layers.sparse import build_neighbor_map, conv_row_order
+    from oracle import sparse_oracle as O
+
+    dev = torch.device("cuda", 0)
+    dt = torch.bfloat16
+    coords_np = scenes.shell_union(64, 4, seed=9, thickness=3.0)
+    n = len(coords_np)
+    coords = torch.from_numpy(coords_np).to(dev)
+    f_np = torch.from_numpy(scenes.normal_features(n, 64, 10)).to(dt).float().numpy()
+    w_np = torch.from_numpy(scenes.conv_weight(32, 64, 3, 11)).to(dt).float().numpy()
+    b_np = torch.linspace(-1, 1, 32).to(dt).float().numpy()
+    feats = torch.from_numpy(f_np).to(dev, dt)
+    w = torch.from_numpy(w_np).to(dev, dt).contiguous()
+    b = torch.from_numpy(b_np).to(dev, dt)
+    nbr = build_neighbor_map(coords, 3)
+    oracle = O.sparse_conv3d(f_np, nbr.cpu().numpy(), O.spconv_weight_to_kio(w_np), b_np)
+    got = torch.full((n, 32), float("nan"), device=dev)
+    flags = torch.full((8,), 1 << 40, dtype=torch.int64, device=dev)  # every flag already raised
+    flag_ptrs = (ctypes.c_void_p * 8)(*[flags.data_ptr() + 8 * i for i in range(8)])
+    halo_total = 0
+    for rank in range(world):
+        plan = HaloPlan.build(coords, nbr, rank, world)
+        halo_total += plan.halo.numel()
+        local = torch.cat([feats[plan.own], feats[plan.halo]]).contiguous()
+        lnbr = plan.local_nbr.to(dev)
+        order, tiles = conv_row_order(lnbr)
+        plain = conv3d_forward(local, lnbr, w, N.SV_WEIGHT_OKI, b, 32, row_order=order,
+                               tile_order=tiles)
+        plan.local_nbr = lnbr
+        interior, boundary = plan.split()
+        plan.split_schedule = (*_subset_schedule(lnbr, interior), *_subset_schedule(lnbr, boundary))
+        rows, tile_list, halo_from = _fused_schedule(plan)
+        fused = torch.empty((plan.num_local, 32), device=dev, dtype=dt)
+        senders = sum(1 for s in range(world) if s != rank and plan.recv_count[s] > 0)
+        conv3d_forward_halo(local, lnbr, w, b, 32, rows, tile_list, halo_from, flag_ptrs,
+                            min(senders, 8), 1, out=fused)
+        N.check_device_status(dev)
+        assert torch.equal(fused[: plan.num_own], plain[: plan.num_own])
+        got[plan.own] = plain[: plan.num_own].float()
+    assert halo_total > 0
+    assert not torch.isnan(got).any(), "a row is owned by no rank"
+    err = np.abs(got.cpu().numpy() - oracle).max() / np.abs(oracle).max()
+    assert err <= 1e-2, err
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
