@@ -50,7 +50,7 @@ def parse_args():
     p.add_argument(
         "--workload",
         choices=["conv1024", "kmap", "pool", "scene128", "sweep", "halo", "topology", "resblock",
-                 "backward", "config1", "hbm"],
+                 "backward", "config1", "hbm", "narrow"],
         default="conv1024",
         help="conv1024 (default): the headline line above. The others run on one GPU and "
         "print one line each: kmap = kernel-map build on 16 x 128^3 at 8%% occupancy; pool = "
@@ -66,7 +66,10 @@ def parse_args():
         "~20k-voxel 64^3 shell (CUDA cores), with the CPU oracle timed beside it; hbm = the "
         "HBM-bound kernels once per step each through the package API (map and pooling on "
         "4 x 128^3 at 8%% with 128 bf16 channels, row norm + SiLU on those rows at 1024 "
-        "channels, subdivide of the coarse tensor, occupancy of 16 x 64^3 fp32 logits)",
+        "channels, subdivide of the coarse tensor, occupancy of 16 x 64^3 fp32 logits); narrow = "
+        "the narrow-channel convs (config 4's scene128, config 3's 128->128, config 5's shell and "
+        "uniform cells at 64/128 channels) with the deduplicated-tile kernel and the "
+        "mask-sorted tcgen05 kernel side by side",
     )
     p.add_argument(
         "--profiling",
@@ -664,10 +667,11 @@ def _hbm_roofline(bytes_per_launch: float, ms: float, kernel: str) -> dict:
             "peak_source": peaks["source"], "algorithmic_bytes": bytes_per_launch}
 
 
-def conv_timing(args, dev, flush, coords, cin, cout, dtype, seed, feats=None):
+def conv_timing(args, dev, flush, coords, cin, cout, dtype, seed, feats=None, algo=None):
     """One cached-map convolution through ``SparseConv3D``: mean device ms, valid pairs, the
     input tensor and its roofline (tensor or HBM bound, whichever is slower at the measured
-    peaks; F = 2 Cin Cout P, B = dt N (Cin + Cout) + dt K Cin Cout + 4 K N)."""
+    peaks; F = 2 Cin Cout P, B = dt N (Cin + Cout) + dt K Cin Cout + 4 K N). ``algo`` forces a
+    kernel (``sv_conv_algo`` or SV_CONV_TCGEN05_DEDUP); AUTO by default."""
 
     import torch
 
@@ -681,6 +685,8 @@ def conv_timing(args, dev, flush, coords, cin, cout, dtype, seed, feats=None):
     conv = SparseConv3D(cin, cout, 3).to(dev)
     conv.conv.weight = torch.from_numpy(scenes.conv_weight(cout, cin, 3, seed + 1)).to(dev, dtype)
     conv.conv.bias = torch.zeros(cout, device=dev, dtype=dtype)
+    if algo is not None:
+        conv.algo = algo
     x = SparseTensor(feats, c, int(coords[:, 0].max()) + 1, None)
     conv(x)  # builds and caches the map and schedule
     nbr = x.cache["neighbors_3_1_(1, 1, 1)"]
@@ -1021,6 +1027,9 @@ def run_workload(args) -> None:
     def map_case(coords):
         return map_timing(args, dev, flush, coords)
 
+    def conv_case_algo(coords, cin, cout, algo):
+        return conv_timing(args, dev, flush, coords, cin, cout, torch.bfloat16, 11, algo=algo)
+
     lines = []
     if args.workload == "kmap":
         coords = scenes.batched([scenes.uniform(128, 0.08, 500 + b) for b in range(16)])
@@ -1103,6 +1112,23 @@ def run_workload(args) -> None:
                             "groups": groups},
                            _hbm_roofline(16.0 * n + 4.0 * n + 4.0 * (groups + 1), ms,
                                          "window grouping (key sort + first-row sort)")))
+    elif args.workload == "narrow":
+        cases = [("scene128", scenes.scene128(0), 64, 64), ("scene128", scenes.scene128(0), 64, 32),
+                 ("shell64x2", scenes.batched([scenes.shell64(3), scenes.shell64(4)]), 128, 128)]
+        for layout, grid, occ in (("shell", 64, 0.08), ("shell", 128, 0.02),
+                                  ("uniform", 128, 0.30), ("uniform", 64, 0.08)):
+            gen = scenes.uniform if layout == "uniform" else scenes.shell_fraction
+            cc = scenes.batched([gen(grid, occ, 700 + b) for b in range(16)])
+            for ch in (64, 128):
+                cases.append((f"{layout}{grid}x16_{occ:g}", cc, ch, ch))
+        for name, coords, cin, cout in cases:
+            for label, algo in (("dedup", N.SV_CONV_TCGEN05_DEDUP), ("mask-sorted", N.SV_CONV_TCGEN05)):
+                ms, pairs, _, roof = conv_case_algo(coords, cin, cout, algo)
+                lines.append(_line("sparse conv3d active-voxels/s", len(coords) / (ms * 1e-3),
+                                   "voxels/s", ms, args,
+                                   {"workload": f"{name}_conv{cin}to{cout}_bf16", "kernel": label,
+                                    "voxels": len(coords), "valid_pairs": pairs,
+                                    "pairs_per_row": pairs / len(coords)}, roof))
     elif args.workload == "hbm":
         lines.extend(hbm_lines(args, dev, flush))
     elif args.workload == "resblock":

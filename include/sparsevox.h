@@ -200,6 +200,32 @@ SV_API int sv_conv3d_forward_halo(const void* features, int64_t n, int cin, cons
                                   int cout, int dtype, void* out, void* workspace,
                                   size_t workspace_bytes, int32_t* status, sv_stream_t stream);
 
+/* ---- narrow-channel convolution on deduplicated tiles ---------------------------------------
+ * The same convolution as sv_conv3d_forward (the Metal kernel of
+ * src/mlx_diffuser/kernels/sparse.py:9-36, reached from SparseConv3D.__call__,
+ * src/mlx_diffuser/layers/sparse.py:217-235) for fp16/bf16 3x3x3 convolutions with Cin = 64 or
+ * 128 and Cout a multiple of 32. Its tiles are 128 rows adjacent in space (Morton order); each
+ * tile's distinct source rows are read from global memory once, into shared memory, and every
+ * A operand is assembled from there into tensor memory. Best on surfaces and dense scenes
+ * (many neighbours per row); sv_conv3d_forward stays better for very sparse maps.
+ *
+ * sv_conv_dd_plan builds the tile plan from the coordinates and the kernel map (cache it with
+ * the map): `plan` holds sv_conv_dd_plan_bytes(n, cin) bytes, 256-byte aligned, and the build
+ * needs sv_conv_dd_plan_workspace_bytes(n) bytes of scratch. sv_conv3d_forward_dd then runs the
+ * convolution (weight in the spconv (Cout, 3, 3, 3, Cin) layout; residual optional as in
+ * sv_conv3d_forward_residual; 4 bytes of workspace for its scheduler). */
+SV_API int sv_conv_dd_supported(int64_t n, int cin, int cout, int kvol, int dtype);
+SV_API size_t sv_conv_dd_plan_bytes(int64_t n, int cin);
+SV_API size_t sv_conv_dd_plan_workspace_bytes(int64_t n);
+SV_API int sv_conv_dd_plan(const int32_t* coords, const int32_t* nbr, int64_t n, int kvol,
+                           int cin, void* plan, size_t plan_bytes, void* workspace,
+                           size_t workspace_bytes, int32_t* status, sv_stream_t stream);
+SV_API int sv_conv3d_forward_dd(const void* features, int64_t n, int cin, const int32_t* nbr,
+                                int kvol, const void* plan, size_t plan_bytes,
+                                const void* weight, const void* bias, const void* residual,
+                                int cout, int dtype, void* out, void* workspace,
+                                size_t workspace_bytes, int32_t* status, sv_stream_t stream);
+
 /* Repack a (K, Cin, Cout) weight into spconv's (Cout, K, Cin) layout. */
 SV_API int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int cout, int dtype,
                                 void* w_oki, sv_stream_t stream);

@@ -31,6 +31,7 @@ SV_WEIGHT_OKI = 1
 SV_CONV_AUTO = 0
 SV_CONV_SIMT = 1
 SV_CONV_TCGEN05 = 2
+SV_CONV_TCGEN05_DEDUP = 3  # Python-level choice: sv_conv_dd_plan + sv_conv3d_forward_dd
 
 # device status bits
 SV_DEVICE_TABLE_FULL = 0x1
@@ -76,6 +77,13 @@ _SIGNATURES = {
         _I32,
         [_P, _I64, _I32, _P, _I32, _P, _I64, _P, _I32, _P, _I32, _I64, _P, _P, _P, _I32, _I32,
          _P, _P, _SZ, _P, _P],
+    ),
+    "sv_conv_dd_supported": (_I32, [_I64, _I32, _I32, _I32, _I32]),
+    "sv_conv_dd_plan_bytes": (_SZ, [_I64, _I32]),
+    "sv_conv_dd_plan_workspace_bytes": (_SZ, [_I64]),
+    "sv_conv_dd_plan": (_I32, [_P, _P, _I64, _I32, _I32, _P, _SZ, _P, _SZ, _P, _P]),
+    "sv_conv3d_forward_dd": (
+        _I32, [_P, _I64, _I32, _P, _I32, _P, _SZ, _P, _P, _P, _I32, _I32, _P, _P, _SZ, _P, _P]
     ),
     "sv_weight_kio_to_oki": (_I32, [_P, _I32, _I32, _I32, _I32, _P, _P]),
     "sv_rownorm": (

@@ -99,6 +99,63 @@ def conv3d_forward(
     return out
 
 
+class DedupPlan:
+    """Tile plan of the deduplicated narrow-channel convolution (``sv_conv_dd_plan``) for one
+    kernel map: 128-row tiles in Morton order, each with its distinct source rows and a local
+    map into them. Built once per map and input width, cached next to the map."""
+
+    def __init__(self, coords: torch.Tensor, neighbors: torch.Tensor, cin: int):
+        n, kvol = neighbors.shape
+        dev = neighbors.device
+        lib = N.load()
+        self.n, self.cin = n, cin
+        self.nbytes = int(lib.sv_conv_dd_plan_bytes(n, cin))
+        self.buffer = torch.empty(max(self.nbytes, 1), dtype=torch.uint8, device=dev)
+        if n == 0:
+            return
+        coords = coords.to(device=dev, dtype=torch.int32).contiguous()
+        ws_bytes = lib.sv_conv_dd_plan_workspace_bytes(n)
+        ws = N.workspace(ws_bytes, dev)
+        rc = lib.sv_conv_dd_plan(coords.data_ptr(), neighbors.data_ptr(), n, kvol, cin,
+                                 self.buffer.data_ptr(), self.nbytes, ws.data_ptr(), ws_bytes,
+                                 N.status_word(dev).data_ptr(), N.stream(dev))
+        N.check(rc, "sparse_conv3d (tile plan)")
+
+
+def dedup_supported(n: int, cin: int, cout: int, kvol: int, dtype: torch.dtype) -> bool:
+    code = N.DTYPE_CODE.get(dtype)
+    return code is not None and bool(N.load().sv_conv_dd_supported(n, cin, cout, kvol, code))
+
+
+def conv3d_forward_dd(features, neighbors, plan: DedupPlan, weight_oki, bias, cout, *,
+                      out=None, residual=None) -> torch.Tensor:
+    """``sv_conv3d_forward_dd``: the narrow-channel tensor-core convolution over a
+    :class:`DedupPlan` (fp16/bf16, 3x3x3, Cin 64 or 128, Cout % 32 == 0). Tensors contiguous
+    on one CUDA device, weight in the spconv (Cout, 3, 3, 3, Cin) layout."""
+
+    n, cin = features.shape
+    dev = features.device
+    if out is None:
+        out = torch.empty((n, cout), dtype=features.dtype, device=dev)
+    if n == 0 or cout == 0:
+        return out
+    if plan.n != n or plan.cin != cin:
+        raise ValueError("tile plan was built for another map or input width")
+    if residual is not None and (tuple(residual.shape) != (n, cout)
+                                 or residual.dtype != features.dtype
+                                 or not residual.is_contiguous()):
+        raise ValueError(f"residual must be a contiguous ({n}, {cout}) {features.dtype} tensor")
+    lib = N.load()
+    ws = N.workspace(256, dev)
+    rc = lib.sv_conv3d_forward_dd(
+        features.data_ptr(), n, cin, neighbors.data_ptr(), neighbors.shape[1],
+        plan.buffer.data_ptr(), plan.nbytes, weight_oki.data_ptr(), N.ptr(bias),
+        N.ptr(residual), cout, N.DTYPE_CODE[features.dtype], out.data_ptr(), ws.data_ptr(), 256,
+        N.status_word(dev).data_ptr(), N.stream(dev))
+    N.check(rc, "sparse_conv3d (deduplicated tiles)")
+    return out
+
+
 def sparse_conv3d(
     features,
     neighbors,
