@@ -75,7 +75,8 @@ SV_API int sv_abi_version(void);
 
 /* Slots of the open-addressing coordinate table used for n rows (a power of two >= 2n). */
 SV_API int64_t sv_kmap_table_slots(int64_t n);
-/* Workspace bytes for sv_kmap_build with `table_slots` slots (4 bytes per slot). */
+/* Workspace bytes for sv_kmap_build with `table_slots` slots (48 bytes per slot: a 3x3x3,
+ * dilation-1 map uses a table of 2x2x2 voxel blocks, other kernels a table of voxels). */
 SV_API size_t sv_kmap_workspace_bytes(int64_t table_slots);
 
 /* nbr[p, k] = the row of (b, c1+d1, c2+d2, c3+d3), or -1, for the offsets (d1, d2, d3) of a
@@ -84,8 +85,9 @@ SV_API size_t sv_kmap_workspace_bytes(int64_t table_slots);
  * coords columns 1, 2, 3. Duplicate coordinate rows resolve to the largest row index.
  * coords: [n, 4] int32 (batch, c1, c2, c3), 16-byte aligned; nbr: [n, kernel volume] int32.
  * The hash table lives in `workspace` (sv_kmap_workspace_bytes(table_slots) bytes). A table
- * with fewer slots than distinct rows is detected on the device: SV_DEVICE_TABLE_FULL is ORed
- * into `status` (the return value only reports what the host can see). */
+ * with fewer slots than the distinct rows (2x2x2 blocks, for a 3x3x3 map) it has to hold is
+ * detected on the device: SV_DEVICE_TABLE_FULL is ORed into `status` (the return value only
+ * reports what the host can see). */
 SV_API int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t kernel[3],
                          const int32_t dilation[3], int32_t* nbr, int64_t table_slots,
                          void* workspace, size_t workspace_bytes, int32_t* status,

@@ -99,6 +99,132 @@ __global__ void kmap_probe_kernel(const int4* __restrict__ coords, int64_t n,
   nbr[idx] = r;
 }
 
+// ---- block table (3x3x3 kernels, dilation 1) ---------------------------------------------------
+// The table holds 2x2x2 blocks of voxels instead of single voxels: a slot is a block's full key
+// (batch, c1 >> 1, c2 >> 1, c3 >> 1) -- 16 bytes, claimed with one 128-bit compare-and-swap --
+// and, in a parallel array, the rows of its 8 cells (32 bytes, cell = (c1 & 1) << 2 |
+// (c2 & 1) << 1 | (c3 & 1)). The 27 neighbours of a voxel lie in exactly 8 blocks (two per axis),
+// so a row's map takes 8 independent key probes instead of 27, each one 16-byte load; neighbouring
+// rows share blocks, so most of those loads hit L1. A duplicate coordinate row resolves to the
+// largest row index (atomicMax on its cell), as with the voxel table and the reference's dict.
+// An empty slot's c1 >> 1 field holds 0x7F7F7F7F, a value an arithmetic shift of an int32 cannot
+// produce, so the keys array is cleared with a byte memset.
+
+constexpr int32_t BLOCK_EMPTY = 0x7F7F7F7F;
+
+__device__ __forceinline__ bool same4(int4 a, int4 b) {
+  return a.x == b.x && a.y == b.y && a.z == b.z && a.w == b.w;
+}
+
+__global__ void kmap_block_insert_kernel(const int4* __restrict__ coords, int64_t n,
+                                         int4* keys, int32_t* cells, uint32_t mask,
+                                         int32_t* status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int4 c = __ldg(&coords[i]);
+  const int4 key = make_int4(c.x, c.y >> 1, c.z >> 1, c.w >> 1);
+  const int cell = ((c.y & 1) << 2) | ((c.z & 1) << 1) | (c.w & 1);
+  uint32_t h = hash_coord(key.x, key.y, key.z, key.w) & mask;
+  const int4 empty = make_int4(BLOCK_EMPTY, BLOCK_EMPTY, BLOCK_EMPTY, BLOCK_EMPTY);
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    // A plain 16-byte read (L2, not L1) may be stale or interleave with another thread's
+    // compare-and-swap of the slot. A read equal to the key is genuine (a mix of old and new
+    // fields cannot equal a key, whose c1, c2, c3 fields are never 0x7F7F7F7F); anything else is
+    // confirmed by the CAS, which returns the slot's value atomically (and claims it when empty).
+    int4 cur = __ldcg(&keys[h]);
+    if (!same4(cur, key)) {
+      cur = atomicCAS(&keys[h], empty, key);
+      if (cur.y == BLOCK_EMPTY) cur = key;  // claimed the empty slot
+    }
+    if (same4(cur, key)) {
+      atomicMax(&cells[(int64_t)h * 8 + cell], (int32_t)i);
+      return;
+    }
+    h = (h + 1) & mask;
+  }
+  report(status, SV_DEVICE_TABLE_FULL);
+}
+
+// Slot of the block `key`, or -1 when no row lies in it.
+__device__ __forceinline__ int64_t block_find(const int4* __restrict__ keys, uint32_t mask,
+                                              int4 key, uint32_t h, int4 first) {
+  int4 cur = first;
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    if (same4(cur, key)) return (int64_t)h;
+    if (cur.y == BLOCK_EMPTY) return -1;
+    h = (h + 1) & mask;
+    cur = __ldg(&keys[h]);
+  }
+  return -1;
+}
+
+// One thread per row (128 per CTA): the 8 blocks around the row are probed together, then the
+// 27 neighbours are read from their cells; the CTA's [128][27] map rows go out through shared
+// memory as contiguous stores.
+__global__ void __launch_bounds__(128)
+    kmap_block_probe_kernel(const int4* __restrict__ coords, int64_t n,
+                            const int4* __restrict__ keys, const int32_t* __restrict__ cells,
+                            uint32_t mask, int32_t* __restrict__ nbr) {
+  __shared__ int32_t stage[128 * 27];
+  const int64_t row0 = (int64_t)blockIdx.x * 128;
+  const int64_t i = row0 + threadIdx.x;
+  if (i < n) {
+    const int4 c = __ldg(&coords[i]);
+    // the two block coordinates along each axis that the offsets -1, 0, +1 reach (a side whose
+    // neighbour leaves the int32 range has no block: its neighbours miss)
+    int32_t g[3][2];
+    bool ok[3][2];
+    const int32_t v3[3] = {c.y, c.z, c.w};
+#pragma unroll
+    for (int a = 0; a < 3; ++a) {
+      const int64_t lo = (int64_t)v3[a] - 1, hi = (int64_t)v3[a] + 1;
+      ok[a][0] = lo >= INT32_MIN;
+      ok[a][1] = hi <= INT32_MAX;
+      g[a][0] = (int32_t)(lo >> 1);
+      g[a][1] = (int32_t)(hi >> 1);
+    }
+    // first probe of all 8 blocks in flight together
+    int4 bkey[8];
+    uint32_t bh[8];
+    int4 first[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      bkey[b] = make_int4(c.x, g[0][b >> 2], g[1][(b >> 1) & 1], g[2][b & 1]);
+      bh[b] = hash_coord(bkey[b].x, bkey[b].y, bkey[b].z, bkey[b].w) & mask;
+      first[b] = __ldg(&keys[bh[b]]);
+    }
+    int64_t slot[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const bool in_range = ok[0][b >> 2] && ok[1][(b >> 1) & 1] && ok[2][b & 1];
+      slot[b] = in_range ? block_find(keys, mask, bkey[b], bh[b], first[b]) : -1;
+    }
+    // offset k = 9 (d1 + 1) + 3 (d2 + 1) + (d3 + 1), the reference's order
+#pragma unroll
+    for (int k = 0; k < 27; ++k) {
+      const int d[3] = {k / 9 - 1, (k / 3) % 3 - 1, k % 3 - 1};
+      int b = 0, cell = 0;
+      bool valid = true;
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        const int64_t v = (int64_t)v3[a] + d[a];
+        valid = valid && v >= INT32_MIN && v <= INT32_MAX;
+        const int32_t gv = (int32_t)(v >> 1);
+        // which of the two blocks along this axis: the upper one when its coordinate differs
+        const int side = (d[a] > 0 || (d[a] == 0 && gv != g[a][0])) ? 1 : 0;
+        b |= side << (2 - a);
+        cell |= (int)(v & 1) << (2 - a);
+      }
+      const int64_t s = slot[b];
+      stage[threadIdx.x * 27 + k] = (valid && s >= 0) ? __ldg(&cells[s * 8 + cell]) : -1;
+    }
+  }
+  __syncthreads();
+  const int64_t rows = min((int64_t)128, n - row0);
+  int32_t* dst = nbr + row0 * 27;
+  for (int j = threadIdx.x; j < rows * 27; j += 128) dst[j] = stage[j];
+}
+
 __global__ void row_mask_kernel(const int32_t* __restrict__ nbr, int64_t n, int kvol,
                                 uint32_t* __restrict__ masks, int32_t* __restrict__ rows) {
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -238,19 +364,19 @@ extern "C" int64_t sv_kmap_table_slots(int64_t n) {
 }
 
 extern "C" size_t sv_kmap_workspace_bytes(int64_t table_slots) {
-  return table_slots > 0 ? (size_t)table_slots * sizeof(int32_t) : 0;
+  // block table: 16-byte keys + 8 four-byte cells per slot (the voxel table needs 4 bytes)
+  return table_slots > 0 ? (size_t)table_slots * 48 : 0;
 }
 
-extern "C" int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t kernel[3],
-                             const int32_t dilation[3], int32_t* nbr, int64_t table_slots,
-                             void* workspace, size_t workspace_bytes, int32_t* status,
-                             sv_stream_t stream) {
+namespace {
+
+int kmap_check(const int32_t* coords, int64_t n, const int32_t kernel[3],
+               const int32_t dilation[3], int32_t* nbr, int64_t table_slots) {
   if (n < 0 || kernel == nullptr || dilation == nullptr)
     SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_kmap_build: bad arguments");
   for (int i = 0; i < 3; ++i)
     if (kernel[i] <= 0 || kernel[i] % 2 == 0)
       SV_FAIL(SV_ERR_BAD_SHAPE, "sparse submanifold kernels must have three odd dimensions");
-  const int64_t kvol = (int64_t)kernel[0] * kernel[1] * kernel[2];
   if (n == 0) return SV_OK;
   if (coords == nullptr || nbr == nullptr)
     SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_kmap_build: null coords or nbr");
@@ -258,10 +384,14 @@ extern "C" int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t ker
   if (!aligned16(coords)) SV_FAIL(SV_ERR_INVALID_ARGUMENT, "coords must be 16-byte aligned");
   if (table_slots < 64 || (table_slots & (table_slots - 1)) != 0 || table_slots > (1ll << 31))
     SV_FAIL(SV_ERR_INVALID_ARGUMENT, "table_slots must be a power of two in [64, 2^31]");
-  if (workspace == nullptr || workspace_bytes < sv_kmap_workspace_bytes(table_slots))
-    SV_FAIL(SV_ERR_WORKSPACE, "sv_kmap_build: workspace too small");
-  cudaStream_t s = to_stream(stream);
-  int32_t* table = static_cast<int32_t*>(workspace);
+  return SV_OK;
+}
+
+// The map through a table of single voxels (4 bytes per slot): any kernel and dilation.
+int kmap_build_voxels(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                      const int32_t dilation[3], int32_t* nbr, int64_t table_slots,
+                      int32_t* table, int32_t* status, cudaStream_t s) {
+  const int64_t kvol = (int64_t)kernel[0] * kernel[1] * kernel[2];
   const uint32_t mask = (uint32_t)(table_slots - 1);
   SV_CUDA_TRY(cudaMemsetAsync(table, 0xFF, (size_t)table_slots * sizeof(int32_t), s));
   const int threads = 256;
@@ -274,6 +404,41 @@ extern "C" int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t ker
       dilation[0], dilation[1], dilation[2], nbr);
   SV_LAUNCH_CHECK();
   return SV_OK;
+}
+
+// The 3x3x3, dilation-1 map through the block table (48 bytes per slot).
+int kmap_build_blocks(const int32_t* coords, int64_t n, int32_t* nbr, int64_t table_slots,
+                      void* workspace, int32_t* status, cudaStream_t s) {
+  const uint32_t mask = (uint32_t)(table_slots - 1);
+  int4* keys = static_cast<int4*>(workspace);
+  int32_t* cells = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + table_slots * 16);
+  SV_CUDA_TRY(cudaMemsetAsync(keys, 0x7F, (size_t)table_slots * 16, s));
+  SV_CUDA_TRY(cudaMemsetAsync(cells, 0xFF, (size_t)table_slots * 32, s));
+  kmap_block_insert_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+      reinterpret_cast<const int4*>(coords), n, keys, cells, mask, status);
+  SV_LAUNCH_CHECK();
+  kmap_block_probe_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(
+      reinterpret_cast<const int4*>(coords), n, keys, cells, mask, nbr);
+  SV_LAUNCH_CHECK();
+  return SV_OK;
+}
+
+}  // namespace
+
+extern "C" int sv_kmap_build(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                             const int32_t dilation[3], int32_t* nbr, int64_t table_slots,
+                             void* workspace, size_t workspace_bytes, int32_t* status,
+                             sv_stream_t stream) {
+  const int rc = kmap_check(coords, n, kernel, dilation, nbr, table_slots);
+  if (rc != SV_OK || n == 0) return rc;
+  if (workspace == nullptr || workspace_bytes < sv_kmap_workspace_bytes(table_slots))
+    SV_FAIL(SV_ERR_WORKSPACE, "sv_kmap_build: workspace too small");
+  cudaStream_t s = to_stream(stream);
+  const bool k333 = kernel[0] == 3 && kernel[1] == 3 && kernel[2] == 3 && dilation[0] == 1 &&
+                    dilation[1] == 1 && dilation[2] == 1;
+  if (k333) return kmap_build_blocks(coords, n, nbr, table_slots, workspace, status, s);
+  return kmap_build_voxels(coords, n, kernel, dilation, nbr, table_slots,
+                           static_cast<int32_t*>(workspace), status, s);
 }
 
 extern "C" int sv_coords_bounds(const int32_t* coords, int64_t n, int32_t* bounds_out,
@@ -467,8 +632,10 @@ extern "C" int sv_kmap_build_static(const int32_t* coords, int64_t n, const int3
     const int rc = static_table_address(to_stream(stream), &table);
     if (rc != SV_OK) return rc;
   }
-  // sv_kmap_build clears the `slots` words it uses to -1 before inserting, so nothing of an
-  // earlier call's table survives into this one.
-  return sv_kmap_build(coords, n, kernel, dilation, nbr, slots, table,
-                       (size_t)slots * sizeof(int32_t), status, stream);
+  // the voxel table (4 bytes per slot) clears the `slots` words it uses to -1 before inserting,
+  // so nothing of an earlier call's table survives into this one
+  const int rc = kmap_check(coords, n, kernel, dilation, nbr, slots);
+  if (rc != SV_OK || n == 0) return rc;
+  return kmap_build_voxels(coords, n, kernel, dilation, nbr, slots, table, status,
+                           to_stream(stream));
 }

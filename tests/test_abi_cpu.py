@@ -46,7 +46,7 @@ def test_abi_version_and_sizes():
     assert lib.sv_abi_version() == 1
     assert lib.sv_kmap_table_slots(0) == 64
     assert lib.sv_kmap_table_slots(1000) == 2048
-    assert lib.sv_kmap_workspace_bytes(2048) == 2048 * 4
+    assert lib.sv_kmap_workspace_bytes(2048) == 2048 * 48
     assert lib.sv_conv_plan_workspace_bytes(0) == 0
     assert lib.sv_downsample_workspace_bytes(10) >= 10 * 28
     # KIO weight on a tensor-core shape needs a repack workspace; OKI needs none

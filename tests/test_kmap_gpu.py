@@ -80,6 +80,28 @@ def test_kmap_edge_cases_match_dict_oracle():
     assert m[7, 13] == 9 and m[9, 13] == 9
 
 
+def test_block_table_edge_values_match_dict_oracle():
+    """The 3x3x3 map goes through the 2x2x2-block table: blocks straddling zero (negative
+    coordinates floor-divide), every corner of the int32 range, a batch index equal to the
+    table's empty marker (0x7F7F7F7F), duplicates spread over several blocks, and a dense random
+    cloud with many duplicates -- all against the reference's dict restated on the CPU."""
+
+    imax, imin = np.iinfo(np.int32).max, np.iinfo(np.int32).min
+    marker = 0x7F7F7F7F
+    rows = [[marker, 0, 0, 0], [marker, 1, 1, 1], [marker, 0, 0, 0], [marker, -1, 0, 0]]
+    for cx in (imin, imin + 1, imax - 1, imax):
+        for cy in (imin, imax):
+            for cz in (imin + 1, imax - 1):
+                rows.append([2, cx, cy, cz])
+    edge = np.array(rows, np.int32)
+    assert np.array_equal(_gpu_map(edge), O.build_neighbor_map_dict(edge, 3))
+    rng = np.random.default_rng(21)
+    cloud = rng.integers(-4, 4, size=(3000, 4)).astype(np.int32)
+    cloud[:, 0] = rng.integers(-2, 2, size=3000)
+    want = O.build_neighbor_map_dict(cloud, 3)
+    assert np.array_equal(_gpu_map(cloud), want)
+
+
 def test_kmap_empty_and_single():
     assert _gpu_map(np.zeros((0, 4), np.int32)).shape == (0, 27)
     single = _gpu_map(np.array([[0, 3, 4, 5]], np.int32))
