@@ -42,13 +42,14 @@ int transpose(const void* in, int64_t rows, int64_t cols, int esize, void* out, 
 
 bool valid_dtype(int d) { return d == SV_FLOAT32 || d == SV_FLOAT16 || d == SV_BFLOAT16; }
 
-// Would the AUTO/TCGEN05 choice take the tensor-core kernel for this shape (after a repack)?
+// Would the AUTO/TCGEN05 choice take a tensor-core kernel for this shape (after a repack)?
+// fp16/bf16 run on conv_tc, fp32 on the 3xTF32 kernel.
 bool tc_path(const ConvArgs& a, int algo) {
   if (algo == SV_CONV_SIMT) return false;
   ConvArgs b = a;
   b.layout = SV_WEIGHT_OKI;  // a KIO weight is repacked into an aligned workspace
   if (a.layout == SV_WEIGHT_KIO) b.weight = reinterpret_cast<const void*>(uintptr_t(256));
-  return conv_tc_supported(b);
+  return a.dtype == SV_FLOAT32 ? conv_tf32_supported(b) : conv_tc_supported(b);
 }
 
 }  // namespace
@@ -75,10 +76,11 @@ extern "C" size_t sv_conv3d_workspace_bytes(int64_t n, int cin, int cout, int kv
   a.layout = layout;
   a.features = a.out = reinterpret_cast<void*>(uintptr_t(256));
   if (!tc_path(a, algo)) return 0;
-  // scheduler word, then (for a KIO weight) the repacked weight
+  // scheduler word, then (for a KIO weight) the repacked weight, then (fp32) its hi/lo halves
   const size_t repack =
       layout == SV_WEIGHT_KIO ? align_up((size_t)kvol * cin * cout * dtype_size(dtype), 256) : 0;
-  return 256 + repack;
+  const size_t split = dtype == SV_FLOAT32 ? conv_tf32_split_bytes(kvol, cin, cout) : 0;
+  return 256 + repack + split;
 }
 
 extern "C" int sv_weight_kio_to_oki(const void* w_kio, int kvol, int cin, int cout, int dtype,
@@ -150,22 +152,27 @@ extern "C" int sv_conv3d_forward_rows(const void* features, int64_t n, int cin,
   const bool use_tc = tc_path(a, algo) && aligned16(weight);
   if (algo == SV_CONV_TCGEN05 && !use_tc)
     SV_FAIL(SV_ERR_UNSUPPORTED,
-            "tcgen05 convolution needs fp16/bf16, Cin % 32 == 0, Cout % 32 == 0, kernel volume "
-            "<= 27 and 16-byte aligned features/weight/out/residual");
+            "tcgen05 convolution needs Cin % 32 == 0, Cout % 32 == 0, kernel volume <= 27 and "
+            "16-byte aligned features/weight/out/residual");
   if (!use_tc) return conv_simt_launch(a, s);
   const size_t need = sv_conv3d_workspace_bytes(n, cin, cout, kvol, dtype, layout, algo);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     SV_FAIL(SV_ERR_WORKSPACE,
             "sv_conv3d_forward: the tcgen05 path needs sv_conv3d_workspace_bytes() of workspace");
   int32_t* counter = static_cast<int32_t*>(workspace);
+  size_t used = 256;
   if (layout == SV_WEIGHT_KIO) {
-    void* packed = static_cast<uint8_t*>(workspace) + 256;
+    void* packed = static_cast<uint8_t*>(workspace) + used;
     int rc = transpose(weight, (int64_t)kvol * cin, cout, dtype_size(dtype), packed, s);
     if (rc != SV_OK) return rc;
     a.weight = packed;
     a.layout = SV_WEIGHT_OKI;
+    used += align_up((size_t)kvol * cin * cout * dtype_size(dtype), 256);
   }
   // tile_order only makes sense together with the row schedule it was derived from
+  if (dtype == SV_FLOAT32)
+    return conv_tf32_launch(a, row_order ? tile_order : nullptr, counter,
+                            static_cast<uint8_t*>(workspace) + used, s);
   return conv_tc_launch(a, row_order ? tile_order : nullptr, counter, s);
 }
 
@@ -189,7 +196,7 @@ extern "C" int sv_conv3d_forward_halo(const void* features, int64_t n, int cin,
     SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_conv3d_forward_halo: null pointer");
   ConvArgs a{features, n, cin, nbr, kvol, rows, weight, SV_WEIGHT_OKI, bias, cout, dtype, out,
              status, residual, n_rows, halo_from_tile, flag_count, epoch, flags};
-  if (!tc_path(a, SV_CONV_TCGEN05) || !aligned16(weight))
+  if (dtype == SV_FLOAT32 || !tc_path(a, SV_CONV_TCGEN05) || !aligned16(weight))
     SV_FAIL(SV_ERR_UNSUPPORTED,
             "sv_conv3d_forward_halo runs on the tcgen05 kernel: fp16/bf16, Cin % 32 == 0, "
             "Cout % 32 == 0, 16-byte aligned operands");

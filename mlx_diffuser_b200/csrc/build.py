@@ -20,7 +20,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, "libsparsevox.so")
-SOURCES = ["api.cu", "kmap.cu", "pool.cu", "topology.cu", "norm.cu", "backward.cu", "wgrad_tc.cu", "halo.cu", "conv_simt.cu", "conv_tc.cu", "conv_dd.cu"]
+SOURCES = ["api.cu", "kmap.cu", "pool.cu", "topology.cu", "norm.cu", "backward.cu", "wgrad_tc.cu", "halo.cu", "conv_simt.cu", "conv_tc.cu", "conv_dd.cu", "conv_tf32.cu"]
 HEADERS = ["common.cuh", "conv.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

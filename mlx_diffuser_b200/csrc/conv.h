@@ -39,4 +39,11 @@ bool conv_tc_supported(const ConvArgs& a);
 int conv_tc_launch(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
                    cudaStream_t s);
 
+// 3xTF32 tcgen05 kernel for fp32 (OKI layout, Cin % 32 == 0, Cout % 32 == 0, K <= 27):
+// `split` holds conv_tf32_split_bytes() of scratch for the weight's hi / lo halves.
+bool conv_tf32_supported(const ConvArgs& a);
+size_t conv_tf32_split_bytes(int kvol, int cin, int cout);
+int conv_tf32_launch(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, void* split,
+                     cudaStream_t s);
+
 }  // namespace sv

@@ -55,7 +55,11 @@ def test_abi_version_and_sizes():
     # the tensor-core path always needs its scheduler word; the CUDA-core path nothing
     assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 2, N.SV_WEIGHT_OKI, N.SV_CONV_AUTO) == 256
     assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 2, N.SV_WEIGHT_OKI, N.SV_CONV_SIMT) == 0
-    assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 0, N.SV_WEIGHT_KIO, N.SV_CONV_AUTO) == 0
+    # fp32 runs on the 3xTF32 kernel: scheduler word, repacked weight, its hi / lo halves
+    w32 = 27 * 64 * 64 * 4
+    assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 0, N.SV_WEIGHT_KIO,
+                                         N.SV_CONV_AUTO) == 256 + 3 * w32
+    assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 0, N.SV_WEIGHT_KIO, N.SV_CONV_SIMT) == 0
     assert lib.sv_conv3d_workspace_bytes(100, 8, 64, 27, 2, N.SV_WEIGHT_KIO, N.SV_CONV_AUTO) == 0
 
 

@@ -114,6 +114,56 @@ def test_tcgen05_shapes(cin, cout, dtype):
     assert max_rel_err(out, ref) <= HALF_TOL
 
 
+@pytest.mark.parametrize("cin,cout", [(32, 32), (64, 96), (128, 128), (96, 64), (160, 256),
+                                      (256, 32)])
+def test_tf32x3_fp32_shapes(cin, cout):
+    """fp32 on the tensor cores (3xTF32) against the oracle at rtol 1e-4, with bias, in both
+    weight layouts, and with a residual. Against a float64 evaluation its max relative error stays
+    below 3e-5 (the CUDA-core fp32 kernel measures ~1e-6 to 1.5e-5 on these shapes; 3xTF32 drops
+    the lo x lo products, ~2^-20 of each product)."""
+
+    coords = scenes.batched(
+        [scenes.shell(16, 5.5, 2.0, 1.0, seed=7), scenes.shell(12, 4.0, 2.0, 0.5, seed=9)]
+    )
+    f = scenes.normal_features(len(coords), cin, seed=1)
+    w = scenes.conv_weight(cout, cin, 3, seed=2)
+    b = (np.random.default_rng(3).standard_normal(cout) * 0.1).astype(np.float32)
+    nbr = O.build_neighbor_map(coords, 3)
+    ref = O.sparse_conv3d(f, nbr, O.spconv_weight_to_kio(w), b, accum=np.float64)
+    out, x = _run(coords, f, w, b, torch.float32, algo=N.SV_CONV_TCGEN05)
+    assert_f32_close(out, ref)
+    assert max_rel_err(out, ref) <= 3e-5
+    simt, _ = _run(coords, f, w, b, torch.float32, algo=N.SV_CONV_SIMT)
+    assert_f32_close(simt, ref)
+    # the functional form with a (K, Cin, Cout) weight, and a residual added in the epilogue
+    nbr_d = x.cache["neighbors_3_1_(1, 1, 1)"]
+    feats = torch.from_numpy(f).to(DEV)
+    wk = torch.from_numpy(O.spconv_weight_to_kio(w)).to(DEV).contiguous()
+    fun = conv3d_forward(feats, nbr_d, wk, N.SV_WEIGHT_KIO, torch.from_numpy(b).to(DEV), cout,
+                         algo=N.SV_CONV_TCGEN05)
+    assert_f32_close(fun.cpu().numpy(), ref)
+    res = torch.from_numpy(scenes.normal_features(len(coords), cout, seed=4)).to(DEV)
+    wo = torch.from_numpy(w).to(DEV).contiguous()
+    with_res = conv3d_forward(feats, nbr_d, wo, N.SV_WEIGHT_OKI, torch.from_numpy(b).to(DEV),
+                              cout, algo=N.SV_CONV_TCGEN05, residual=res)
+    assert_f32_close(with_res.cpu().numpy(), ref + res.cpu().numpy())
+    N.check_device_status(DEV)
+
+
+def test_tf32x3_config1_every_row():
+    """Config 1 (64^3 shell, ~20k rows, 128 -> 128, fp32) on the 3xTF32 kernel: every row
+    against the fp32 oracle at rtol 1e-4, several persistent work items per CTA."""
+
+    coords = scenes.shell64(0)
+    f = scenes.normal_features(len(coords), 128, seed=1)
+    w = scenes.conv_weight(128, 128, 3, seed=2)
+    b = np.zeros(128, np.float32)
+    out, x = _run(coords, f, w, b, torch.float32, algo=N.SV_CONV_TCGEN05)
+    nbr = x.cache["neighbors_3_1_(1, 1, 1)"].cpu().numpy()
+    assert np.array_equal(nbr, O.build_neighbor_map(coords, 3))
+    assert_f32_close(out, O.sparse_conv3d(f, nbr, O.spconv_weight_to_kio(w), b, accum=np.float64))
+
+
 @pytest.mark.parametrize("cin,cout", [(64, 64), (64, 128), (64, 256), (32, 32), (32, 256)])
 def test_tcgen05_persistent_ctas_take_several_items(cin, cout):
     """24k rows give more work items than SMs, so each persistent CTA runs several items and
