@@ -59,7 +59,8 @@ typedef enum sv_dtype { SV_FLOAT32 = 0, SV_FLOAT16 = 1, SV_BFLOAT16 = 2 } sv_dty
 typedef enum sv_weight_layout { SV_WEIGHT_KIO = 0, SV_WEIGHT_OKI = 1 } sv_weight_layout;
 
 /* Convolution algorithm. AUTO picks a tcgen05 tensor-core kernel when the shape allows it
- * (Cin % 32 == 0, Cout % 32 == 0, K <= 27, 16-byte aligned pointers) -- fp16/bf16 directly,
+ * (Cin and Cout multiples of 32 -- or, for fp16/bf16, 8 or 16 --, K <= 27, 16-byte aligned
+ * pointers) -- fp16/bf16 directly,
  * fp32 as 3xTF32 (each operand split into a TF32 high part and an fp32 remainder; three
  * products per K step) -- and the CUDA-core kernel otherwise. */
 typedef enum sv_conv_algo { SV_CONV_AUTO = 0, SV_CONV_SIMT = 1, SV_CONV_TCGEN05 = 2 } sv_conv_algo;

@@ -9,7 +9,12 @@
 // groups rows with equal neighbour masks) x BN output channels. Its K loop visits only the
 // offsets for which at least one of its 128 rows has a neighbour -- the union of the rows'
 // masks -- and within an offset walks Cin in BK-channel stages (BK = 64 with the 128-byte
-// swizzle, or 32 with the 64-byte swizzle when Cin is an odd multiple of 32).
+// swizzle, or 32 with the 64-byte swizzle when Cin is an odd multiple of 32). Inputs of 8 or 16
+// channels pack PACK = 32 / Cin consecutive offsets into one 32-channel stage: their weight
+// columns are adjacent in the spconv (Cout, K*Cin) matrix, so B stays one TMA box (past the last
+// offset it reads TMA's zero fill), and each 16-byte A chunk gathers a different offset's
+// neighbour. Outputs of 8 or 16 channels run as N = 16 tiles (the smallest MMA N at M = 128)
+// whose weight rows past Cout are TMA zero fill; the epilogue stores Cout columns.
 //
 // Persistent CTAs (one per SM) take work items from an atomic counter. Items run one
 // BN-wide slab of output channels at a time (so one slab of weights is live in L2), and within
@@ -152,7 +157,7 @@ __device__ __forceinline__ void decode_item(const Sched& sc, int32_t item, int32
   *n0 = nt * BN;
 }
 
-template <int BN, int BK, typename T, bool kResidual>
+template <int BN, int BK, typename T, bool kResidual, int PACK>
 __global__ void __launch_bounds__(TTHREADS, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T* __restrict__ feat,
                    int n, int cin, const int32_t* __restrict__ nbr, int kvol,
@@ -183,7 +188,9 @@ __global__ void __launch_bounds__(TTHREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int kb_per_k = cin / BK;
+  // stages per mask bit: Cin / BK blocks of one offset, or (PACK > 1) one stage per bit, a bit
+  // standing for a group of PACK offsets
+  const int kb_per_k = PACK > 1 ? 1 : cin / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -232,7 +239,7 @@ __global__ void __launch_bounds__(TTHREADS, 1)
             }
             mbar_arrive_expect_tx(&full[slot], L::B_STAGE_BYTES);
             tma_load_2d(smem_u32(sB + slot * L::B_STAGE_BYTES), &tmap_w, &full[slot],
-                        k * cin + kb * BK, w.n0);
+                        PACK > 1 ? k * BK : k * cin + kb * BK, w.n0);
           }
         }
       }
@@ -312,10 +319,15 @@ __global__ void __launch_bounds__(TTHREADS, 1)
         const int k = __ffs(m) - 1;
         const T* src[PASSES];
         uint32_t nbytes[PASSES];
+        // packed stages: chunk c belongs to offset PACK * k + c / CPC of the group k, and is
+        // part c % CPC of that neighbour's CPC-chunk row; otherwise chunk c of offset k's row
+        constexpr int CPC = PACK > 1 ? CPR / PACK : CPR;
+        const int kc = PACK > 1 ? PACK * k + (int)chunk / CPC : k;
+        const uint32_t part = PACK > 1 ? chunk % CPC : chunk;
 #pragma unroll
         for (int i = 0; i < PASSES; ++i) {
-          const int32_t s_row = nb[(row0 + RPP * i) * TMAX_KVOL + k];
-          src[i] = feat + (s_row >= 0 ? (int64_t)s_row * cin : 0) + chunk * 8;
+          const int32_t s_row = kc < kvol ? nb[(row0 + RPP * i) * TMAX_KVOL + kc] : -1;
+          src[i] = feat + (s_row >= 0 ? (int64_t)s_row * cin : 0) + part * 8;
           nbytes[i] = s_row >= 0 ? 16u : 0u;
         }
         for (int kb = 0; kb < kb_per_k; ++kb, ++it) {
@@ -358,6 +370,41 @@ __global__ void __launch_bounds__(TTHREADS, 1)
       tc_fence_after();
       const int32_t orow = s_orow[ws * TBM + er];
       const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+      if constexpr (BN < 32) {
+        // an N = 16 tile: Cout (8 or 16) columns stored, as 16-byte vectors
+        uint32_t v[16];
+        if (w.umask != 0) {
+          tmem_ld_32x32b_x16(t_row, v);
+          tc_wait_ld();
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0u;
+        }
+        const int nc = min(BN, cout - w.n0);
+        if (orow >= 0 && nc > 0) {
+          uint32_t packed[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float lo = __uint_as_float(v[2 * j]);
+            float hi = __uint_as_float(v[2 * j + 1]);
+            if (2 * j < nc) {
+              if (bias) {
+                lo += to_f32(bias[w.n0 + 2 * j]);
+                hi += to_f32(bias[w.n0 + 2 * j + 1]);
+              }
+              if constexpr (kResidual) {
+                const T* rrow = residual + (int64_t)orow * cout + w.n0;
+                lo += to_f32(rrow[2 * j]);
+                hi += to_f32(rrow[2 * j + 1]);
+              }
+            }
+            packed[j] = pack2<T>(lo, hi);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)orow * cout + w.n0);
+          dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          if (nc > 8) dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        }
+      }
 #pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
         uint32_t v[32];
@@ -477,7 +524,14 @@ __global__ void __launch_bounds__(TTHREADS, 1)
         WorkSlot w;
         w.item = (valid && !fail) ? item : -1;
         w.n0 = n0;
-        w.umask = s_wmask[0] | s_wmask[1] | s_wmask[2] | s_wmask[3];
+        uint32_t um = s_wmask[0] | s_wmask[1] | s_wmask[2] | s_wmask[3];
+        if (PACK > 1) {  // bit g: some row has a neighbour among offsets PACK*g .. PACK*g+PACK-1
+          uint32_t gm = 0;
+          for (int g = 0; g * PACK < TMAX_KVOL; ++g)
+            gm |= (uint32_t)(((um >> (g * PACK)) & ((1u << PACK) - 1u)) != 0) << g;
+          um = gm;
+        }
+        w.umask = um;
         w.pad = 0;
         slots[ws] = w;
         mbar_arrive(&work_full[ws]);
@@ -532,7 +586,7 @@ int weight_map(const ConvArgs& a, bool bf16, int box_k, int box_rows, CUtensorMa
   return SV_OK;
 }
 
-template <int BN, int BK, typename T, bool kResidual>
+template <int BN, int BK, typename T, bool kResidual, int PACK>
 int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
   using L = TcLayout<BN, BK>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -540,7 +594,7 @@ int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cu
   SV_CUDA_TRY(cudaGetDevice(&dev));
   static bool attr_done[256] = {};
   if (dev >= 256 || !attr_done[dev]) {
-    SV_CUDA_TRY(cudaFuncSetAttribute(conv_tc_kernel<BN, BK, T, kResidual>,
+    SV_CUDA_TRY(cudaFuncSetAttribute(conv_tc_kernel<BN, BK, T, kResidual, PACK>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
     if (dev < 256) attr_done[dev] = true;
   }
@@ -557,13 +611,13 @@ int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cu
   sc.wait_count = a.wait_count;
   sc.wait_epoch = a.wait_epoch;
   for (int i = 0; i < 8; ++i) sc.wait_flags[i] = i < a.wait_count ? a.wait_flags[i] : nullptr;
-  sc.n_tiles = a.cout / BN;
+  sc.n_tiles = (a.cout + BN - 1) / BN;  // an N = 16 tile covers Cout = 8 too
   const int64_t items = (int64_t)sc.row_tiles * sc.n_tiles;
   if (items > INT32_MAX / 2) SV_FAIL(SV_ERR_UNSUPPORTED, "too many tensor-core work items");
   const int grid = (int)std::min<int64_t>(items, num_sms());
   sc.total_items = (int32_t)items;
   SV_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int32_t), s));
-  conv_tc_kernel<BN, BK, T, kResidual><<<grid, TTHREADS, L::SMEM, s>>>(
+  conv_tc_kernel<BN, BK, T, kResidual, PACK><<<grid, TTHREADS, L::SMEM, s>>>(
       tmap, static_cast<const T*>(a.features), (int)a.n, a.cin, a.nbr, a.kvol,
       a.row_order, static_cast<const T*>(a.bias), static_cast<const T*>(a.residual), a.cout,
       static_cast<T*>(a.out), sc, a.status);
@@ -571,19 +625,22 @@ int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cu
   return SV_OK;
 }
 
-template <int BK, typename T, bool kResidual>
+template <int BK, typename T, bool kResidual, int PACK>
 int launch_bk(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
-  if (a.cout % 256 == 0) return launch_bn<256, BK, T, kResidual>(a, tile_order, counter, s);
-  if (a.cout % 128 == 0) return launch_bn<128, BK, T, kResidual>(a, tile_order, counter, s);
-  if (a.cout % 64 == 0) return launch_bn<64, BK, T, kResidual>(a, tile_order, counter, s);
-  return launch_bn<32, BK, T, kResidual>(a, tile_order, counter, s);
+  if (a.cout < 32) return launch_bn<16, BK, T, kResidual, PACK>(a, tile_order, counter, s);
+  if (a.cout % 256 == 0) return launch_bn<256, BK, T, kResidual, PACK>(a, tile_order, counter, s);
+  if (a.cout % 128 == 0) return launch_bn<128, BK, T, kResidual, PACK>(a, tile_order, counter, s);
+  if (a.cout % 64 == 0) return launch_bn<64, BK, T, kResidual, PACK>(a, tile_order, counter, s);
+  return launch_bn<32, BK, T, kResidual, PACK>(a, tile_order, counter, s);
 }
 
 template <typename T, bool kResidual>
 int launch_res(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
                cudaStream_t s) {
-  if (a.cin % 64 == 0) return launch_bk<64, T, kResidual>(a, tile_order, counter, s);
-  return launch_bk<32, T, kResidual>(a, tile_order, counter, s);
+  if (a.cin == 8) return launch_bk<32, T, kResidual, 4>(a, tile_order, counter, s);
+  if (a.cin == 16) return launch_bk<32, T, kResidual, 2>(a, tile_order, counter, s);
+  if (a.cin % 64 == 0) return launch_bk<64, T, kResidual, 1>(a, tile_order, counter, s);
+  return launch_bk<32, T, kResidual, 1>(a, tile_order, counter, s);
 }
 
 template <typename T>
@@ -597,7 +654,8 @@ int launch_typed(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
 
 bool conv_tc_supported(const ConvArgs& a) {
   return (a.dtype == SV_FLOAT16 || a.dtype == SV_BFLOAT16) && a.layout == SV_WEIGHT_OKI &&
-         a.cin > 0 && a.cin % 32 == 0 && a.cout > 0 && a.cout % 32 == 0 && a.kvol >= 1 &&
+         a.cin > 0 && (a.cin % 32 == 0 || a.cin == 8 || a.cin == 16) && a.cout > 0 &&
+         (a.cout % 32 == 0 || a.cout == 8 || a.cout == 16) && a.kvol >= 1 &&
          a.kvol <= TMAX_KVOL && a.n <= INT32_MAX - TBM && (int64_t)a.kvol * a.cin < INT32_MAX &&
          aligned16(a.features) && aligned16(a.weight) && aligned16(a.out) &&
          aligned16(a.residual);

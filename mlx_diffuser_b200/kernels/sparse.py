@@ -3,8 +3,8 @@
 Drop-in for ``mlx_diffuser.kernels.sparse`` (``src/mlx_diffuser/kernels/sparse.py``): the same
 function name, arguments, validation and errors, computing what the reference's Metal kernel
 computes (``:9-36``) -- fp32 accumulation, one rounding to the feature dtype -- with the
-library's tcgen05 kernels when Cin % 32 == 0 and Cout % 32 == 0 (fp16/bf16 directly, fp32 as
-3xTF32) or its CUDA-core kernel (everything else). ``use_metal`` is accepted for signature compatibility; there is one
+library's tcgen05 kernels when Cin and Cout are multiples of 32 (fp16/bf16 directly, fp32 as
+3xTF32; fp16/bf16 also with 8 or 16 channels) or its CUDA-core kernel (everything else). ``use_metal`` is accepted for signature compatibility; there is one
 (CUDA) implementation and no CPU fallback.
 """
 

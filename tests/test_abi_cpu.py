@@ -60,7 +60,11 @@ def test_abi_version_and_sizes():
     assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 0, N.SV_WEIGHT_KIO,
                                          N.SV_CONV_AUTO) == 256 + 3 * w32
     assert lib.sv_conv3d_workspace_bytes(100, 64, 64, 27, 0, N.SV_WEIGHT_KIO, N.SV_CONV_SIMT) == 0
-    assert lib.sv_conv3d_workspace_bytes(100, 8, 64, 27, 2, N.SV_WEIGHT_KIO, N.SV_CONV_AUTO) == 0
+    # 8 input channels run on the tensor cores too (offsets packed four per stage)
+    assert lib.sv_conv3d_workspace_bytes(100, 8, 64, 27, 2, N.SV_WEIGHT_KIO,
+                                         N.SV_CONV_AUTO) == 256 + 27 * 8 * 64 * 2
+    # 24 input channels: the CUDA-core kernel, no workspace
+    assert lib.sv_conv3d_workspace_bytes(100, 24, 64, 27, 2, N.SV_WEIGHT_KIO, N.SV_CONV_AUTO) == 0
 
 
 def test_argument_errors_are_reported_before_any_launch():

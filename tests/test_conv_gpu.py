@@ -114,6 +114,52 @@ def test_tcgen05_shapes(cin, cout, dtype):
     assert max_rel_err(out, ref) <= HALF_TOL
 
 
+@pytest.mark.parametrize("cin,cout", [(8, 128), (16, 64), (128, 8), (64, 16), (8, 8), (16, 16),
+                                      (8, 32), (256, 8)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tcgen05_small_channels(cin, cout, dtype):
+    """8 or 16 channels on the tensor cores: 32 / Cin offsets packed into one K stage, N = 16
+    tiles for 8 or 16 outputs (the I/O convolutions of the SLat stack)."""
+
+    coords = scenes.batched(
+        [scenes.shell(16, 5.5, 2.0, 1.0, seed=7), scenes.shell(12, 4.0, 2.0, 0.5, seed=9)]
+    )
+    f = _rounded(scenes.normal_features(len(coords), cin, seed=1), dtype)
+    w = _rounded(scenes.conv_weight(cout, cin, 3, seed=2), dtype)
+    b = _rounded(np.random.default_rng(3).standard_normal(cout).astype(np.float32) * 0.1, dtype)
+    nbr = O.build_neighbor_map(coords, 3)
+    ref = O.sparse_conv3d(f, nbr, O.spconv_weight_to_kio(w), b)
+    out, x = _run(coords, f, w, b, dtype, algo=N.SV_CONV_TCGEN05)
+    assert max_rel_err(out, ref) <= HALF_TOL
+    # with a residual added in the epilogue
+    nbr_d = x.cache["neighbors_3_1_(1, 1, 1)"]
+    res = _rounded(scenes.normal_features(len(coords), cout, seed=4), dtype)
+    got = conv3d_forward(x.features, nbr_d, torch.from_numpy(w).to(DEV, dtype).contiguous(),
+                         N.SV_WEIGHT_OKI, torch.from_numpy(b).to(DEV, dtype), cout,
+                         algo=N.SV_CONV_TCGEN05, residual=torch.from_numpy(res).to(DEV, dtype))
+    assert max_rel_err(got.float().cpu().numpy(), ref + res) <= HALF_TOL
+    N.check_device_status(DEV)
+
+
+def test_tcgen05_packed_offsets_past_the_kernel_volume():
+    """A 3 x 1 x 3 kernel (9 offsets) at 8 input channels: the third group of 4 packed offsets
+    holds offset 8 and three that do not exist, which must contribute nothing."""
+
+    coords = scenes.shell(16, 5.5, 2.0, 1.0, seed=5)
+    dtype = torch.bfloat16
+    c = torch.from_numpy(coords).to(DEV)
+    nbr = build_neighbor_map(c, (3, 1, 3))
+    f = _rounded(scenes.normal_features(len(coords), 8, seed=6), dtype)
+    w = _rounded(np.random.default_rng(7).standard_normal((64, 9, 8)) / np.sqrt(72), dtype)
+    ref = O.sparse_conv3d(f, nbr.cpu().numpy(), np.ascontiguousarray(w.transpose(1, 2, 0)),
+                          np.zeros(64, np.float32))
+    out = conv3d_forward(torch.from_numpy(f).to(DEV, dtype), nbr,
+                         torch.from_numpy(w).to(DEV, dtype).contiguous(), N.SV_WEIGHT_OKI, None, 64,
+                         algo=N.SV_CONV_TCGEN05)
+    N.check_device_status(DEV)
+    assert max_rel_err(out.float().cpu().numpy(), ref) <= HALF_TOL
+
+
 @pytest.mark.parametrize("cin,cout", [(32, 32), (64, 96), (128, 128), (96, 64), (160, 256),
                                       (256, 32)])
 def test_tf32x3_fp32_shapes(cin, cout):
