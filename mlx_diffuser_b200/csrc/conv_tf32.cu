@@ -578,6 +578,8 @@ int launch_tf32_bn(const ConvArgs& a, const float* w_hi, const float* w_lo,
 template <bool kResidual>
 int launch_tf32(const ConvArgs& a, const float* w_hi, const float* w_lo,
                 const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
+  // the widest slab: A (gathered and split per item) is the expensive operand, so halving the
+  // slab to fill the last wave costs more than the wave's tail (measured on config 1)
   if (a.cout % 128 == 0)
     return launch_tf32_bn<128, kResidual>(a, w_hi, w_lo, tile_order, counter, s);
   if (a.cout % 64 == 0)
