@@ -130,6 +130,16 @@ SV_API int sv_kmap_build_grid(const int32_t* coords, int64_t n, const int32_t ke
                               const int64_t extent[4], void* workspace, size_t workspace_bytes,
                               int32_t* status, sv_stream_t stream);
 
+/* The same map with the table chosen on the device, no host synchronisation: from 2^17 rows the
+ * kernels read the coordinates' bounding box on the GPU and build a dense grid when the box holds
+ * at most 16 cells per row (and fits the workspace), the hash table of sv_kmap_build otherwise
+ * (sv_kmap_table_slots(n) slots); fewer rows always take the hash table. The map is the same
+ * either way. Workspace: sv_kmap_auto_workspace_bytes(n), 16-byte aligned. */
+SV_API size_t sv_kmap_auto_workspace_bytes(int64_t n);
+SV_API int sv_kmap_build_auto(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                              const int32_t dilation[3], int32_t* nbr, void* workspace,
+                              size_t workspace_bytes, int32_t* status, sv_stream_t stream);
+
 /* Schedule for the tensor-core convolution, derived from a kernel map:
  *  row_order [n]: a permutation of 0..n-1 that groups rows with equal neighbour-validity masks
  *                 (stable, so rows with one mask keep their spatial order);

@@ -55,6 +55,8 @@ _SIGNATURES = {
     "sv_coords_bounds": (_I32, [_P, _I64, _P, _P, _SZ, _P]),
     "sv_kmap_grid_workspace_bytes": (_SZ, [_P]),
     "sv_kmap_build_grid": (_I32, [_P, _I64, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
+    "sv_kmap_auto_workspace_bytes": (_SZ, [_I64]),
+    "sv_kmap_build_auto": (_I32, [_P, _I64, _P, _P, _P, _P, _SZ, _P, _P]),
     "sv_conv_plan_tiles": (_I64, [_I64]),
     "sv_conv_plan_workspace_bytes": (_SZ, [_I64]),
     "sv_conv_plan": (_I32, [_P, _I64, _I32, _P, _P, _P, _SZ, _P]),

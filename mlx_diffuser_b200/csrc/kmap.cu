@@ -13,6 +13,7 @@
 #include <mutex>
 #include <string>
 
+#include <cub/block/block_radix_sort.cuh>
 #include <cub/device/device_radix_sort.cuh>
 
 #include "common.cuh"
@@ -38,11 +39,8 @@ __device__ __forceinline__ bool same(int4 a, int b, int x, int y, int z) {
   return a.x == b && a.y == x && a.z == y && a.w == z;
 }
 
-__global__ void kmap_insert_kernel(const int4* __restrict__ coords, int64_t n, int32_t* table,
-                                   uint32_t mask, int32_t* status) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const int4 c = __ldg(&coords[i]);
+__device__ __forceinline__ void voxel_insert(const int4* __restrict__ coords, int64_t i, int4 c,
+                                             int32_t* table, uint32_t mask, int32_t* status) {
   uint32_t h = hash_coord(c.x, c.y, c.z, c.w) & mask;
   for (uint32_t probe = 0; probe <= mask; ++probe) {
     int32_t cur = *((volatile int32_t*)&table[h]);
@@ -61,6 +59,12 @@ __global__ void kmap_insert_kernel(const int4* __restrict__ coords, int64_t n, i
   report(status, SV_DEVICE_TABLE_FULL);
 }
 
+__global__ void kmap_insert_kernel(const int4* __restrict__ coords, int64_t n, int32_t* table,
+                                   uint32_t mask, int32_t* status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) voxel_insert(coords, i, __ldg(&coords[i]), table, mask, status);
+}
+
 __device__ __forceinline__ int32_t kmap_lookup(const int4* __restrict__ coords,
                                                const int32_t* __restrict__ table, uint32_t mask,
                                                int b, int x, int y, int z) {
@@ -74,6 +78,24 @@ __device__ __forceinline__ int32_t kmap_lookup(const int4* __restrict__ coords,
   return -1;
 }
 
+// The neighbour of row coordinate q at offset k of a kernel (k0, k1, k2) with dilation
+// (d0, d1, d2), in the reference's order; false when it leaves the int32 range (a miss, as a
+// dict lookup of that tuple would be).
+__device__ __forceinline__ bool offset_coord(int4 q, int k, int k0, int k1, int k2, int d0, int d1,
+                                             int d2, int32_t* x, int32_t* y, int32_t* z) {
+  const int c = k % k2;
+  const int b = (k / k2) % k1;
+  const int a = k / (k1 * k2);
+  const int64_t xx = (int64_t)q.y + (int64_t)(a - k0 / 2) * d0;
+  const int64_t yy = (int64_t)q.z + (int64_t)(b - k1 / 2) * d1;
+  const int64_t zz = (int64_t)q.w + (int64_t)(c - k2 / 2) * d2;
+  *x = (int32_t)xx;
+  *y = (int32_t)yy;
+  *z = (int32_t)zz;
+  return xx >= INT32_MIN && xx <= INT32_MAX && yy >= INT32_MIN && yy <= INT32_MAX &&
+         zz >= INT32_MIN && zz <= INT32_MAX;
+}
+
 // One thread per (row, offset): writes nbr row-major, so consecutive threads store
 // consecutive words.
 __global__ void kmap_probe_kernel(const int4* __restrict__ coords, int64_t n,
@@ -84,59 +106,45 @@ __global__ void kmap_probe_kernel(const int4* __restrict__ coords, int64_t n,
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= n * kvol) return;
   const int64_t p = idx / kvol;
-  const int k = (int)(idx - p * kvol);
-  const int c = k % k2;
-  const int b = (k / k2) % k1;
-  const int a = k / (k1 * k2);
   const int4 q = __ldg(&coords[p]);
-  const int64_t x = (int64_t)q.y + (int64_t)(a - k0 / 2) * d0;
-  const int64_t y = (int64_t)q.z + (int64_t)(b - k1 / 2) * d1;
-  const int64_t z = (int64_t)q.w + (int64_t)(c - k2 / 2) * d2;
-  int32_t r = -1;
-  if (x >= INT32_MIN && x <= INT32_MAX && y >= INT32_MIN && y <= INT32_MAX && z >= INT32_MIN &&
-      z <= INT32_MAX)
-    r = kmap_lookup(coords, table, mask, q.x, (int)x, (int)y, (int)z);
+  int32_t x, y, z, r = -1;
+  if (offset_coord(q, (int)(idx - p * kvol), k0, k1, k2, d0, d1, d2, &x, &y, &z))
+    r = kmap_lookup(coords, table, mask, q.x, x, y, z);
   nbr[idx] = r;
 }
 
 // ---- block table (3x3x3 kernels, dilation 1) ---------------------------------------------------
-// The table holds 2x2x2 blocks of voxels instead of single voxels: a slot is a block's full key
-// (batch, c1 >> 1, c2 >> 1, c3 >> 1) -- 16 bytes, claimed with one 128-bit compare-and-swap --
-// and, in a parallel array, the rows of its 8 cells (32 bytes, cell = (c1 & 1) << 2 |
-// (c2 & 1) << 1 | (c3 & 1)). The 27 neighbours of a voxel lie in exactly 8 blocks (two per axis),
-// so a row's map takes 8 independent key probes instead of 27, each one 16-byte load; neighbouring
-// rows share blocks, so most of those loads hit L1. A duplicate coordinate row resolves to the
-// largest row index (atomicMax on its cell), as with the voxel table and the reference's dict.
-// An empty slot's c1 >> 1 field holds 0x7F7F7F7F, a value an arithmetic shift of an int32 cannot
-// produce, so the keys array is cleared with a byte memset.
+// The table holds 2x2x2 blocks of voxels instead of single voxels: slot h is the block's key
+// keys[h] (16 bytes, claimed with one 128-bit compare-and-swap) and, in a parallel array, the
+// rows of its 8 cells cells[h][0..7] (32 bytes, one sector; cell = (c1 & 1) << 2 |
+// (c2 & 1) << 1 | (c3 & 1)). The 27 neighbours of a voxel lie in exactly 8 blocks (two per axis).
+// A duplicate coordinate row resolves to the largest row index (atomicMax on its cell), as with
+// the voxel table and the reference's dict.
+//
+// Key = (batch, (c1 >> 1) + 2^30, (c2 >> 1) + 2^30, (c3 >> 1) + 2^30): an arithmetic shift of an
+// int32 lies in [-2^30, 2^30), so the three coordinate fields lie in [0, 2^31) and are never -1;
+// one 0xFF byte memset of keys and cells leaves every slot empty (key field -1) with cells -1.
 
-constexpr int32_t BLOCK_EMPTY = 0x7F7F7F7F;
+constexpr int32_t BLOCK_BIAS = 0x40000000;
 
 __device__ __forceinline__ bool same4(int4 a, int4 b) {
   return a.x == b.x && a.y == b.y && a.z == b.z && a.w == b.w;
 }
 
-__global__ void kmap_block_insert_kernel(const int4* __restrict__ coords, int64_t n,
-                                         int4* keys, int32_t* cells, uint32_t mask,
-                                         int32_t* status) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const int4 c = __ldg(&coords[i]);
-  const int4 key = make_int4(c.x, c.y >> 1, c.z >> 1, c.w >> 1);
+__device__ __forceinline__ int4 block_key(int32_t b, int32_t g1, int32_t g2, int32_t g3) {
+  return make_int4(b, g1 + BLOCK_BIAS, g2 + BLOCK_BIAS, g3 + BLOCK_BIAS);
+}
+
+__device__ __forceinline__ void block_insert(const int4 c, int64_t i, int4* keys, int32_t* cells,
+                                             uint32_t mask, int32_t* status) {
+  const int4 key = block_key(c.x, c.y >> 1, c.z >> 1, c.w >> 1);
   const int cell = ((c.y & 1) << 2) | ((c.z & 1) << 1) | (c.w & 1);
   uint32_t h = hash_coord(key.x, key.y, key.z, key.w) & mask;
-  const int4 empty = make_int4(BLOCK_EMPTY, BLOCK_EMPTY, BLOCK_EMPTY, BLOCK_EMPTY);
+  const int4 empty = make_int4(-1, -1, -1, -1);
   for (uint32_t probe = 0; probe <= mask; ++probe) {
-    // A plain 16-byte read (L2, not L1) may be stale or interleave with another thread's
-    // compare-and-swap of the slot. A read equal to the key is genuine (a mix of old and new
-    // fields cannot equal a key, whose c1, c2, c3 fields are never 0x7F7F7F7F); anything else is
-    // confirmed by the CAS, which returns the slot's value atomically (and claims it when empty).
-    int4 cur = __ldcg(&keys[h]);
-    if (!same4(cur, key)) {
-      cur = atomicCAS(&keys[h], empty, key);
-      if (cur.y == BLOCK_EMPTY) cur = key;  // claimed the empty slot
-    }
-    if (same4(cur, key)) {
+    // the compare-and-swap returns the slot's key atomically, and claims the slot when empty
+    const int4 cur = atomicCAS(&keys[h], empty, key);
+    if (cur.y == -1 || same4(cur, key)) {
       atomicMax(&cells[(int64_t)h * 8 + cell], (int32_t)i);
       return;
     }
@@ -145,84 +153,153 @@ __global__ void kmap_block_insert_kernel(const int4* __restrict__ coords, int64_
   report(status, SV_DEVICE_TABLE_FULL);
 }
 
-// Slot of the block `key`, or -1 when no row lies in it.
-__device__ __forceinline__ int64_t block_find(const int4* __restrict__ keys, uint32_t mask,
-                                              int4 key, uint32_t h, int4 first) {
-  int4 cur = first;
-  for (uint32_t probe = 0; probe <= mask; ++probe) {
-    if (same4(cur, key)) return (int64_t)h;
-    if (cur.y == BLOCK_EMPTY) return -1;
-    h = (h + 1) & mask;
-    cur = __ldg(&keys[h]);
-  }
-  return -1;
+__global__ void kmap_block_insert_kernel(const int4* __restrict__ coords, int64_t n, int4* keys,
+                                         int32_t* cells, uint32_t mask, int32_t* status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) block_insert(__ldg(&coords[i]), i, keys, cells, mask, status);
 }
 
-// One thread per row (128 per CTA): the 8 blocks around the row are probed together, then the
-// 27 neighbours are read from their cells; the CTA's [128][27] map rows go out through shared
-// memory as contiguous stores.
-__global__ void __launch_bounds__(128)
-    kmap_block_probe_kernel(const int4* __restrict__ coords, int64_t n,
-                            const int4* __restrict__ keys, const int32_t* __restrict__ cells,
-                            uint32_t mask, int32_t* __restrict__ nbr) {
-  __shared__ int32_t stage[128 * 27];
-  const int64_t row0 = (int64_t)blockIdx.x * 128;
-  const int64_t i = row0 + threadIdx.x;
-  if (i < n) {
-    const int4 c = __ldg(&coords[i]);
-    // the two block coordinates along each axis that the offsets -1, 0, +1 reach (a side whose
-    // neighbour leaves the int32 range has no block: its neighbours miss)
-    int32_t g[3][2];
-    bool ok[3][2];
-    const int32_t v3[3] = {c.y, c.z, c.w};
+// The probes run one thread per row. Along an axis the row's two blocks (sides 0 and 1) cover
+// the 4 consecutive coordinates from 2 ((v - 1) >> 1), and the neighbours v - 1, v, v + 1 are 3 of
+// them starting at 1 - (v & 1); so the 8 blocks' cells form a 4x4x4 cube and the 27 neighbours are
+// the 3x3x3 window at (1 - (c1 & 1), 1 - (c2 & 1), 1 - (c3 & 1)), picked with selects on the
+// three parities. Block s = 4 s1 + 2 s2 + s3 of a row has coordinates ((v - 1) >> 1) + s per axis;
+// one whose coordinates leave the int32 range holds no row, and a neighbour whose coordinate
+// leaves the range always falls in such a block.
+constexpr int PROBE_ROWS = 128;  // rows (threads) per CTA
+
+__device__ __forceinline__ int cell_of(const int4& lo, const int4& hi, int c) {
+  switch (c) {
+    case 0: return lo.x;
+    case 1: return lo.y;
+    case 2: return lo.z;
+    case 3: return lo.w;
+    case 4: return hi.x;
+    case 5: return hi.y;
+    case 6: return hi.z;
+    default: return hi.w;
+  }
+}
+
+// The row's 27 map entries from its 8 blocks' cells, in the reference's offset order
+// k = 9 (d1 + 1) + 3 (d2 + 1) + (d3 + 1).
+__device__ __forceinline__ void emit_window(int4 c, const int4 (&lo)[8], const int4 (&hi)[8],
+                                            int32_t* row_stage) {
+  const bool odd0 = c.y & 1, odd1 = c.z & 1, odd2 = c.w & 1;
+  int w1[3][4][4];  // c1 resolved
 #pragma unroll
-    for (int a = 0; a < 3; ++a) {
-      const int64_t lo = (int64_t)v3[a] - 1, hi = (int64_t)v3[a] + 1;
-      ok[a][0] = lo >= INT32_MIN;
-      ok[a][1] = hi <= INT32_MAX;
-      g[a][0] = (int32_t)(lo >> 1);
-      g[a][1] = (int32_t)(hi >> 1);
-    }
-    // first probe of all 8 blocks in flight together
-    int4 bkey[8];
-    uint32_t bh[8];
-    int4 first[8];
+  for (int x = 0; x < 3; ++x)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      bkey[b] = make_int4(c.x, g[0][b >> 2], g[1][(b >> 1) & 1], g[2][b & 1]);
-      bh[b] = hash_coord(bkey[b].x, bkey[b].y, bkey[b].z, bkey[b].w) & mask;
-      first[b] = __ldg(&keys[bh[b]]);
-    }
-    int64_t slot[8];
+    for (int y = 0; y < 4; ++y)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      const bool in_range = ok[0][b >> 2] && ok[1][(b >> 1) & 1] && ok[2][b & 1];
-      slot[b] = in_range ? block_find(keys, mask, bkey[b], bh[b], first[b]) : -1;
-    }
-    // offset k = 9 (d1 + 1) + 3 (d2 + 1) + (d3 + 1), the reference's order
-#pragma unroll
-    for (int k = 0; k < 27; ++k) {
-      const int d[3] = {k / 9 - 1, (k / 3) % 3 - 1, k % 3 - 1};
-      int b = 0, cell = 0;
-      bool valid = true;
-#pragma unroll
-      for (int a = 0; a < 3; ++a) {
-        const int64_t v = (int64_t)v3[a] + d[a];
-        valid = valid && v >= INT32_MIN && v <= INT32_MAX;
-        const int32_t gv = (int32_t)(v >> 1);
-        // which of the two blocks along this axis: the upper one when its coordinate differs
-        const int side = (d[a] > 0 || (d[a] == 0 && gv != g[a][0])) ? 1 : 0;
-        b |= side << (2 - a);
-        cell |= (int)(v & 1) << (2 - a);
+      for (int z = 0; z < 4; ++z) {
+        const int b0 = ((x >> 1) << 2) | ((y >> 1) << 1) | (z >> 1);
+        const int b1 = (((x + 1) >> 1) << 2) | ((y >> 1) << 1) | (z >> 1);
+        const int l0 = ((x & 1) << 2) | ((y & 1) << 1) | (z & 1);
+        const int l1 = (((x + 1) & 1) << 2) | ((y & 1) << 1) | (z & 1);
+        w1[x][y][z] = odd0 ? cell_of(lo[b0], hi[b0], l0) : cell_of(lo[b1], hi[b1], l1);
       }
-      const int64_t s = slot[b];
-      stage[threadIdx.x * 27 + k] = (valid && s >= 0) ? __ldg(&cells[s * 8 + cell]) : -1;
+  int w2[3][3][4];  // c2 resolved
+#pragma unroll
+  for (int x = 0; x < 3; ++x)
+#pragma unroll
+    for (int y = 0; y < 3; ++y)
+#pragma unroll
+      for (int z = 0; z < 4; ++z) w2[x][y][z] = odd1 ? w1[x][y][z] : w1[x][y + 1][z];
+#pragma unroll
+  for (int x = 0; x < 3; ++x)
+#pragma unroll
+    for (int y = 0; y < 3; ++y)
+#pragma unroll
+      for (int z = 0; z < 3; ++z)
+        row_stage[x * 9 + y * 3 + z] = odd2 ? w2[x][y][z] : w2[x][y][z + 1];
+}
+
+// Lower block coordinate along each axis, (v - 1) >> 1, and whether each side lies in range.
+struct RowBlocks {
+  int64_t g[3];
+  bool ok[3][2];
+};
+
+__device__ __forceinline__ RowBlocks row_blocks(int4 c) {
+  RowBlocks rb;
+  const int32_t v3[3] = {c.y, c.z, c.w};
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+    rb.g[a] = ((int64_t)v3[a] - 1) >> 1;
+    rb.ok[a][0] = v3[a] != INT32_MIN;  // v - 1 stays in range
+    rb.ok[a][1] = v3[a] != INT32_MAX;  // v + 1 stays in range
+  }
+  return rb;
+}
+
+// The CTA's [PROBE_ROWS][27] map rows go out through shared memory as contiguous stores.
+__device__ __forceinline__ void flush_rows(const int32_t* stage, int64_t n, int64_t row0,
+                                           int32_t* __restrict__ nbr) {
+  __syncthreads();
+  const int64_t rows = min((int64_t)PROBE_ROWS, n - row0);
+  int32_t* dst = nbr + row0 * 27;
+  for (int j = threadIdx.x; j < rows * 27; j += blockDim.x) dst[j] = stage[j];
+}
+
+// A row's 8 blocks from the block table: all 8 home slots (key and cells) load together, then a
+// block not in its home slot walks the keys.
+__device__ __forceinline__ void block_probe_row(int4 c, const int4* __restrict__ keys,
+                                                const int4* __restrict__ cells4, uint32_t mask,
+                                                int32_t* row_stage) {
+  const RowBlocks rb = row_blocks(c);
+  int4 key[8], k0[8], lo[8], hi[8];
+  uint32_t h0[8];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const int s0 = b >> 2, s1 = (b >> 1) & 1, s2 = b & 1;
+    const bool in = rb.ok[0][s0] && rb.ok[1][s1] && rb.ok[2][s2];
+    key[b] = block_key(c.x, (int32_t)(rb.g[0] + s0), (int32_t)(rb.g[1] + s1),
+                       (int32_t)(rb.g[2] + s2));
+    h0[b] = hash_coord(key[b].x, key[b].y, key[b].z, key[b].w) & mask;
+    k0[b] = make_int4(-1, -1, -1, -1);
+    lo[b] = k0[b];
+    hi[b] = k0[b];
+    if (in) {
+      k0[b] = __ldg(&keys[h0[b]]);
+      lo[b] = __ldg(&cells4[2 * (int64_t)h0[b]]);
+      hi[b] = __ldg(&cells4[2 * (int64_t)h0[b] + 1]);
     }
   }
-  __syncthreads();
-  const int64_t rows = min((int64_t)128, n - row0);
-  int32_t* dst = nbr + row0 * 27;
-  for (int j = threadIdx.x; j < rows * 27; j += 128) dst[j] = stage[j];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    if (same4(k0[b], key[b])) continue;
+    const int4 none = make_int4(-1, -1, -1, -1);
+    int4 l = none, u = none;
+    if (k0[b].y != -1) {  // occupied by another block: walk on until the key or an empty slot
+      uint32_t h = h0[b];
+      for (uint32_t probe = 1; probe <= mask; ++probe) {
+        h = (h + 1) & mask;
+        const int4 k = __ldg(&keys[h]);
+        if (k.y == -1) break;
+        if (same4(k, key[b])) {
+          l = __ldg(&cells4[2 * (int64_t)h]);
+          u = __ldg(&cells4[2 * (int64_t)h + 1]);
+          break;
+        }
+      }
+    }
+    lo[b] = l;
+    hi[b] = u;
+  }
+  emit_window(c, lo, hi, row_stage);
+}
+
+__global__ void __launch_bounds__(PROBE_ROWS)
+    kmap_block_probe_kernel(const int4* __restrict__ coords, int64_t n,
+                            const int4* __restrict__ keys, const int4* __restrict__ cells4,
+                            uint32_t mask, int32_t* __restrict__ nbr) {
+  __shared__ int32_t stage[PROBE_ROWS * 27];
+  const int64_t row0 = (int64_t)blockIdx.x * PROBE_ROWS;
+  if (row0 + threadIdx.x < n)
+    block_probe_row(__ldg(&coords[row0 + threadIdx.x]), keys, cells4, mask,
+                    stage + threadIdx.x * 27);
+  flush_rows(stage, n, row0, nbr);
 }
 
 __global__ void row_mask_kernel(const int32_t* __restrict__ nbr, int64_t n, int kvol,
@@ -251,6 +328,174 @@ __global__ void tile_cost_kernel(const uint32_t* __restrict__ masks_sorted, int6
     keys[t] = 32u - (uint32_t)__popc(u);
     ids[t] = (int32_t)t;
   }
+}
+
+// ---- one-cluster schedule for small maps -----------------------------------------------------
+// Up to PLAN_SMALL_ROWS rows the schedule is one launch of a single thread-block cluster, one CTA
+// per run of PLAN_RUN consecutive rows:
+//   1. each CTA sorts its run's masks (with the row ids) by a block radix sort in registers and
+//      shared memory -- stable, so rows of equal masks keep ascending row order -- and publishes
+//      the sorted keys;
+//   2. after a cluster barrier every CTA copies all runs' sorted keys into shared memory and
+//      places each of its rows by merge rank: its rank in its own run, plus the rows of earlier
+//      runs with a key <= its own, plus the rows of later runs with a key < its own (binary
+//      searches). That is the position a stable sort of all rows gives. The row's mask is ORed
+//      into its 128-row tile's union in global memory;
+//   3. after a second barrier CTA 0 orders the tiles by a stable counting rank of their keys
+//      32 - popcount(union) (ascending, ties by tile id), the order the device-wide pair sort of
+//      the large path gives.
+// A device-wide sort takes a histogram pass, a scan and four onesweep passes of a few
+// microseconds each however few rows there are; this replaces them and the tile sort.
+// 256 threads x 16 rows per run: a block radix sort's cost grows with the rows one CTA sorts
+// (measured on B200: 4096 rows ~19 us, 8192 rows ~31 us), so more, shorter runs merge faster.
+constexpr int PLAN_THREADS = 256;
+constexpr int PLAN_ITEMS = 16;
+constexpr int PLAN_RUN = PLAN_THREADS * PLAN_ITEMS;
+constexpr int PLAN_MAX_RUNS = 8;  // the portable cluster size
+constexpr int PLAN_SMALL_ROWS = PLAN_RUN * PLAN_MAX_RUNS;
+
+using PlanSort = cub::BlockRadixSort<uint32_t, PLAN_THREADS, PLAN_ITEMS, int32_t>;
+
+__device__ __forceinline__ void plan_cluster_sync() {
+  __threadfence();  // global writes of this thread before the barrier's release
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(PLAN_THREADS, 1)
+    plan_small_kernel(const uint32_t* __restrict__ masks, int n, int kvol, uint32_t* run_keys,
+                      uint32_t* tile_union, int32_t* __restrict__ row_order,
+                      int32_t* __restrict__ tile_order) {
+  extern __shared__ __align__(16) uint8_t plan_smem[];
+  const int r = blockIdx.x;  // the grid is one cluster
+  const int runs = gridDim.x;
+  const int t = threadIdx.x;
+  const int tiles = (n + 127) / 128;
+  if (r == 0)
+    for (int j = t; j < tiles; j += PLAN_THREADS) tile_union[j] = 0;
+  // rows past n sort last: the largest key over the sorted bits, and after any real row of that
+  // key by stability (they lie in the last run, after every real row)
+  const uint32_t pad = kvol >= 32 ? 0xFFFFFFFFu : (1u << kvol) - 1u;
+  uint32_t key[PLAN_ITEMS];
+  int32_t val[PLAN_ITEMS];
+#pragma unroll
+  for (int i = 0; i < PLAN_ITEMS; ++i) {
+    const int idx = r * PLAN_RUN + t * PLAN_ITEMS + i;
+    key[i] = idx < n ? __ldg(&masks[idx]) : pad;
+    val[i] = idx;
+  }
+  PlanSort(*reinterpret_cast<PlanSort::TempStorage*>(plan_smem)).Sort(key, val, 0, kvol);
+  uint4* mine = reinterpret_cast<uint4*>(run_keys + r * PLAN_RUN + t * PLAN_ITEMS);
+#pragma unroll
+  for (int i = 0; i < PLAN_ITEMS / 4; ++i)
+    mine[i] = make_uint4(key[4 * i], key[4 * i + 1], key[4 * i + 2], key[4 * i + 3]);
+  plan_cluster_sync();
+
+  // all runs' sorted keys into shared memory, eight 16-byte loads in flight per thread
+  uint32_t* all = reinterpret_cast<uint32_t*>(plan_smem);
+  const uint4* src = reinterpret_cast<const uint4*>(run_keys);
+  const int words4 = runs * PLAN_RUN / 4;
+  for (int j0 = 0; j0 < words4; j0 += 8 * PLAN_THREADS) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u * PLAN_THREADS + t;
+      if (j < words4) v[u] = __ldcg(&src[j]);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u * PLAN_THREADS + t;
+      if (j < words4) reinterpret_cast<uint4*>(all)[j] = v[u];
+    }
+  }
+  __syncthreads();
+  // merge ranks, the thread's rows searched together in each other run
+  int pos[PLAN_ITEMS];
+#pragma unroll
+  for (int i = 0; i < PLAN_ITEMS; ++i) pos[i] = t * PLAN_ITEMS + i;
+  for (int rr = 0; rr < runs; ++rr) {
+    if (rr == r) continue;
+    const uint32_t* run = all + rr * PLAN_RUN;
+    const bool inclusive = rr < r;
+    int lo[PLAN_ITEMS];
+#pragma unroll
+    for (int i = 0; i < PLAN_ITEMS; ++i) lo[i] = 0;
+#pragma unroll
+    for (int step = PLAN_RUN >> 1; step > 0; step >>= 1) {
+#pragma unroll
+      for (int i = 0; i < PLAN_ITEMS; ++i) {
+        const uint32_t v = run[lo[i] + step - 1];
+        if (v < key[i] || (inclusive && v == key[i])) lo[i] += step;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PLAN_ITEMS; ++i) {
+      const uint32_t v = run[lo[i]];
+      pos[i] += lo[i] + ((v < key[i] || (inclusive && v == key[i])) ? 1 : 0);
+    }
+  }
+  // rows out, and each tile's union of masks (ORed per tile locally first)
+  uint32_t acc = 0;
+  int acc_tile = -1;
+#pragma unroll
+  for (int i = 0; i < PLAN_ITEMS; ++i) {
+    if (pos[i] >= n) continue;
+    row_order[pos[i]] = val[i];
+    const int tile = pos[i] >> 7;
+    if (tile != acc_tile) {
+      if (acc_tile >= 0 && tile_order != nullptr) atomicOr(&tile_union[acc_tile], acc);
+      acc_tile = tile;
+      acc = 0;
+    }
+    acc |= key[i];
+  }
+  if (acc_tile >= 0 && tile_order != nullptr) atomicOr(&tile_union[acc_tile], acc);
+  plan_cluster_sync();
+  if (r != 0 || tile_order == nullptr) return;
+
+  uint32_t* tkey = all;  // the merged keys are no longer needed
+  for (int j = t; j < tiles; j += PLAN_THREADS)
+    tkey[j] = 32u - (uint32_t)__popc(__ldcg(&tile_union[j]));
+  __syncthreads();
+  for (int j = t; j < tiles; j += PLAN_THREADS) {
+    const uint32_t kj = tkey[j];
+    int rank = 0;
+    for (int m = 0; m < tiles; ++m) {
+      const uint32_t km = tkey[m];
+      rank += (km < kj) || (km == kj && m < j);
+    }
+    tile_order[rank] = j;
+  }
+}
+
+size_t plan_small_smem(int runs) {
+  return std::max(sizeof(PlanSort::TempStorage), (size_t)runs * PLAN_RUN * 4);
+}
+
+// masks: n row masks; scratch: PLAN_SMALL_ROWS words of run keys and the tile unions after them
+// (16-byte aligned).
+int launch_plan_small(const uint32_t* masks, int64_t n, int kvol, uint32_t* scratch,
+                      int32_t* row_order, int32_t* tile_order, cudaStream_t s) {
+  const int runs = (int)((n + PLAN_RUN - 1) / PLAN_RUN);
+  const size_t smem = plan_small_smem(runs);
+  SV_CUDA_TRY(cudaFuncSetAttribute(plan_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)plan_small_smem(PLAN_MAX_RUNS)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(runs);
+  cfg.blockDim = dim3(PLAN_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = runs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SV_CUDA_TRY(cudaLaunchKernelEx(&cfg, plan_small_kernel, masks, (int)n, kvol, scratch,
+                                 scratch + PLAN_SMALL_ROWS, row_order, tile_order));
+  return SV_OK;
 }
 
 // ---- direct-indexed grid -------------------------------------------------------------------
@@ -291,16 +536,29 @@ __global__ void bounds4_kernel(const int4* __restrict__ coords, int64_t n, int32
       mx[j] = max(mx[j], v[j]);
     }
   }
+  // warp, then CTA reduction: one atomic per CTA and value (atomics from every warp on the same
+  // 8 words serialise in L2)
+  __shared__ int32_t part[8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     mn[j] = __reduce_min_sync(0xffffffffu, mn[j]);
     mx[j] = __reduce_max_sync(0xffffffffu, mx[j]);
   }
-  if ((threadIdx.x & 31) == 0) {
+  if (lane == 0) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      atomicMin(&bounds[j], mn[j]);
-      atomicMax(&bounds[4 + j], mx[j]);
+      part[j][warp] = mn[j];
+      part[4 + j][warp] = mx[j];
+    }
+  }
+  __syncthreads();
+  if (warp < 8) {
+    int32_t v = lane < warps ? part[warp][lane] : (warp < 4 ? INT32_MAX : INT32_MIN);
+    v = warp < 4 ? __reduce_min_sync(0xffffffffu, v) : __reduce_max_sync(0xffffffffu, v);
+    if (lane == 0) {
+      if (warp < 4) atomicMin(&bounds[warp], v);
+      else atomicMax(&bounds[warp], v);
     }
   }
 }
@@ -345,6 +603,171 @@ __global__ void grid_probe_kernel(const int4* __restrict__ coords, int64_t n, Gr
   nbr[idx] = r;
 }
 
+// ---- automatic choice on the device ------------------------------------------------------------
+// sv_kmap_build_auto reads the coordinates' bounding box on the device. Every later kernel of the
+// build derives from those 8 words the same choice, with no host synchronisation: a dense grid
+// when the box holds at most AUTO_GRID_CELLS_PER_ROW cells per row and fits the workspace, the hash
+// table (block table for 3x3x3 dilation-1 maps, voxel table otherwise) when it does not. For a
+// 3x3x3 dilation-1 map the grid is one of 2x2x2 blocks, laid out like the block table's cells
+// (8 rows in one 32-byte sector per block, blocks in (batch, c1 >> 1, c2 >> 1, c3 >> 1) order),
+// so a row's 27 neighbours are 8 sectors; otherwise a grid of single voxels.
+constexpr int64_t AUTO_GRID_CELLS_PER_ROW = 16;
+constexpr int64_t AUTO_GRID_MIN_ROWS = 1 << 17;
+constexpr size_t AUTO_HEADER = 256;  // bytes before the table: the bounds words
+
+struct AutoPlan {
+  bool grid;
+  GridBox g;  // voxel grid: cells; block grid: blocks (batch extent in rows, c1..c3 in blocks)
+  int64_t cells;
+};
+
+__device__ __forceinline__ AutoPlan auto_plan(const int32_t* __restrict__ bounds, int64_t n,
+                                              int64_t cap_cells, bool blocks) {
+  AutoPlan p;
+  p.cells = blocks ? 8 : 1;
+  p.grid = true;
+  const int64_t limit = min(cap_cells, AUTO_GRID_CELLS_PER_ROW * n);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    int32_t lo = __ldg(&bounds[j]), hi = __ldg(&bounds[4 + j]);
+    if (blocks && j > 0) {
+      lo >>= 1;
+      hi >>= 1;
+    }
+    const int64_t ext = (int64_t)hi - lo + 1;
+    p.g.lo[j] = lo;
+    p.g.ext[j] = ext;
+    if (p.grid && ext >= 1 && p.cells <= limit / ext) p.cells *= ext;
+    else p.grid = false;
+  }
+  return p;
+}
+
+// Fills the grid (cells x 4 bytes) or the hash table (hash_bytes) with 0xFF bytes.
+__global__ void auto_clear_kernel(const int32_t* __restrict__ bounds, int64_t n, int64_t cap_cells,
+                                  bool blocks, int4* region, int64_t hash_bytes) {
+  const AutoPlan p = auto_plan(bounds, n, cap_cells, blocks);
+  const int64_t words4 = ((p.grid ? p.cells * 4 : hash_bytes) + 15) / 16;
+  const int4 ones = make_int4(-1, -1, -1, -1);
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < words4;
+       j += (int64_t)gridDim.x * blockDim.x)
+    region[j] = ones;
+}
+
+// Index of block (b, g1, g2, g3) in the block grid, or -1 outside the box.
+__device__ __forceinline__ int64_t grid_block(const GridBox& g, int64_t b, int64_t g1, int64_t g2,
+                                              int64_t g3) {
+  b -= g.lo[0];
+  g1 -= g.lo[1];
+  g2 -= g.lo[2];
+  g3 -= g.lo[3];
+  if ((uint64_t)b >= (uint64_t)g.ext[0] || (uint64_t)g1 >= (uint64_t)g.ext[1] ||
+      (uint64_t)g2 >= (uint64_t)g.ext[2] || (uint64_t)g3 >= (uint64_t)g.ext[3])
+    return -1;
+  return ((b * g.ext[1] + g1) * g.ext[2] + g2) * g.ext[3] + g3;
+}
+
+__global__ void auto_insert_kernel(const int4* __restrict__ coords, int64_t n,
+                                   const int32_t* __restrict__ bounds, int64_t cap_cells,
+                                   void* region, int64_t slots, bool blocks, int32_t* status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const AutoPlan p = auto_plan(bounds, n, cap_cells, blocks);
+  const int4 c = __ldg(&coords[i]);
+  const uint32_t mask = (uint32_t)(slots - 1);
+  int32_t* grid = static_cast<int32_t*>(region);
+  if (p.grid && blocks) {
+    const int64_t blk = grid_block(p.g, c.x, c.y >> 1, c.z >> 1, c.w >> 1);
+    const int cell = ((c.y & 1) << 2) | ((c.z & 1) << 1) | (c.w & 1);
+    if (blk >= 0) atomicMax(grid + blk * 8 + cell, (int32_t)i);
+    else report(status, SV_DEVICE_BAD_INDEX);  // outside its own bounding box: cannot happen
+  } else if (p.grid) {
+    int64_t cell;
+    if (grid_cell(p.g, c.x, c.y, c.z, c.w, &cell)) atomicMax(grid + cell, (int32_t)i);
+    else report(status, SV_DEVICE_BAD_INDEX);
+  } else if (blocks) {
+    int4* keys = static_cast<int4*>(region);
+    block_insert(c, i, keys, reinterpret_cast<int32_t*>(keys + slots), mask, status);
+  } else {
+    voxel_insert(coords, i, c, grid, mask, status);
+  }
+}
+
+// 3x3x3, dilation 1: one thread per row, as kmap_block_probe_kernel; the row's 8 blocks come from
+// the block grid (one sector each, the index of block s is that of block 0 plus s's steps) or
+// from the block table.
+__global__ void __launch_bounds__(PROBE_ROWS)
+    auto_probe333_kernel(const int4* __restrict__ coords, int64_t n,
+                         const int32_t* __restrict__ bounds, int64_t cap_cells,
+                         const void* __restrict__ region, int64_t slots,
+                         int32_t* __restrict__ nbr) {
+  __shared__ int32_t stage[PROBE_ROWS * 27];
+  const AutoPlan p = auto_plan(bounds, n, cap_cells, true);
+  const int64_t row0 = (int64_t)blockIdx.x * PROBE_ROWS;
+  if (row0 + threadIdx.x < n) {
+    const int4 c = __ldg(&coords[row0 + threadIdx.x]);
+    int32_t* row_stage = stage + threadIdx.x * 27;
+    if (p.grid) {
+      const RowBlocks rb = row_blocks(c);
+      // block 0 relative to the box; side s along an axis is in the box when 0 <= rel + s < ext
+      int64_t rel[3];
+      bool in[3][2];
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        rel[a] = rb.g[a] - p.g.lo[a + 1];
+#pragma unroll
+        for (int sd = 0; sd < 2; ++sd)
+          in[a][sd] = rb.ok[a][sd] && (uint64_t)(rel[a] + sd) < (uint64_t)p.g.ext[a + 1];
+      }
+      const int64_t s3 = p.g.ext[3], s2 = p.g.ext[2] * s3;
+      const int64_t base = (((int64_t)c.x - p.g.lo[0]) * p.g.ext[1] + rel[0]) * s2 +
+                           rel[1] * s3 + rel[2];
+      const int4* grid4 = static_cast<const int4*>(region);
+      int4 lo[8], hi[8];
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        const int s0 = b >> 2, s1 = (b >> 1) & 1, sb = b & 1;
+        lo[b] = make_int4(-1, -1, -1, -1);
+        hi[b] = lo[b];
+        if (in[0][s0] && in[1][s1] && in[2][sb]) {
+          const int64_t blk = base + s0 * s2 + s1 * s3 + sb;
+          lo[b] = __ldg(grid4 + 2 * blk);
+          hi[b] = __ldg(grid4 + 2 * blk + 1);
+        }
+      }
+      emit_window(c, lo, hi, row_stage);
+    } else {
+      const int4* keys = static_cast<const int4*>(region);
+      block_probe_row(c, keys, keys + slots, (uint32_t)(slots - 1), row_stage);
+    }
+  }
+  flush_rows(stage, n, row0, nbr);
+}
+
+// Any kernel and dilation: one thread per (row, offset), on the grid or the voxel table.
+__global__ void auto_probe_kernel(const int4* __restrict__ coords, int64_t n,
+                                  const int32_t* __restrict__ bounds, int64_t cap_cells,
+                                  const int32_t* __restrict__ region, int64_t slots, int k0,
+                                  int k1, int k2, int d0, int d1, int d2,
+                                  int32_t* __restrict__ nbr) {
+  const int kvol = k0 * k1 * k2;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * kvol) return;
+  const AutoPlan p = auto_plan(bounds, n, cap_cells, false);
+  const int64_t row = idx / kvol;
+  const int4 q = __ldg(&coords[row]);
+  int32_t x, y, z, r = -1;
+  if (offset_coord(q, (int)(idx - row * kvol), k0, k1, k2, d0, d1, d2, &x, &y, &z)) {
+    if (p.grid) {
+      int64_t cell;
+      if (grid_cell(p.g, q.x, x, y, z, &cell)) r = __ldg(&region[cell]);
+    } else {
+      r = kmap_lookup(coords, region, (uint32_t)(slots - 1), q.x, x, y, z);
+    }
+  }
+  nbr[idx] = r;
+}
+
 size_t plan_cub_bytes(int64_t n) {
   size_t bytes = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
@@ -358,13 +781,15 @@ size_t plan_cub_bytes(int64_t n) {
 using namespace sv;
 
 extern "C" int64_t sv_kmap_table_slots(int64_t n) {
+  // at least 2 slots per row: a load factor of at most 1/2 for the voxel table (one slot per
+  // distinct row) and for the block table (one slot per occupied block, at most one per row)
   int64_t slots = 64;
   while (slots < 2 * n) slots <<= 1;
   return slots;
 }
 
 extern "C" size_t sv_kmap_workspace_bytes(int64_t table_slots) {
-  // block table: 16-byte keys + 8 four-byte cells per slot (the voxel table needs 4 bytes)
+  // block table: a 16-byte key and 8 four-byte cells per slot (the voxel table needs 4 bytes)
   return table_slots > 0 ? (size_t)table_slots * 48 : 0;
 }
 
@@ -411,14 +836,14 @@ int kmap_build_blocks(const int32_t* coords, int64_t n, int32_t* nbr, int64_t ta
                       void* workspace, int32_t* status, cudaStream_t s) {
   const uint32_t mask = (uint32_t)(table_slots - 1);
   int4* keys = static_cast<int4*>(workspace);
-  int32_t* cells = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + table_slots * 16);
-  SV_CUDA_TRY(cudaMemsetAsync(keys, 0x7F, (size_t)table_slots * 16, s));
-  SV_CUDA_TRY(cudaMemsetAsync(cells, 0xFF, (size_t)table_slots * 32, s));
+  int4* cells4 = keys + table_slots;
+  SV_CUDA_TRY(cudaMemsetAsync(keys, 0xFF, (size_t)table_slots * 48, s));
   kmap_block_insert_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
-      reinterpret_cast<const int4*>(coords), n, keys, cells, mask, status);
+      reinterpret_cast<const int4*>(coords), n, keys, reinterpret_cast<int32_t*>(cells4), mask,
+      status);
   SV_LAUNCH_CHECK();
-  kmap_block_probe_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(
-      reinterpret_cast<const int4*>(coords), n, keys, cells, mask, nbr);
+  kmap_block_probe_kernel<<<(unsigned)((n + PROBE_ROWS - 1) / PROBE_ROWS), PROBE_ROWS, 0, s>>>(
+      reinterpret_cast<const int4*>(coords), n, keys, cells4, mask, nbr);
   SV_LAUNCH_CHECK();
   return SV_OK;
 }
@@ -518,6 +943,63 @@ extern "C" int sv_kmap_build_grid(const int32_t* coords, int64_t n, const int32_
   return SV_OK;
 }
 
+extern "C" size_t sv_kmap_auto_workspace_bytes(int64_t n) {
+  if (n <= 0) return 0;
+  const size_t hash = sv_kmap_workspace_bytes(sv_kmap_table_slots(n));
+  const size_t grid = align_up((size_t)(AUTO_GRID_CELLS_PER_ROW * n) * 4, 16);
+  return AUTO_HEADER + std::max(hash, grid);
+}
+
+extern "C" int sv_kmap_build_auto(const int32_t* coords, int64_t n, const int32_t kernel[3],
+                                  const int32_t dilation[3], int32_t* nbr, void* workspace,
+                                  size_t workspace_bytes, int32_t* status, sv_stream_t stream) {
+  const int64_t slots = sv_kmap_table_slots(n);
+  const int rc = kmap_check(coords, n, kernel, dilation, nbr, slots);
+  if (rc != SV_OK || n == 0) return rc;
+  if (workspace == nullptr || workspace_bytes < sv_kmap_auto_workspace_bytes(n))
+    SV_FAIL(SV_ERR_WORKSPACE, "sv_kmap_build_auto: workspace too small");
+  if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+    SV_FAIL(SV_ERR_INVALID_ARGUMENT, "sv_kmap_build_auto: workspace must be 16-byte aligned");
+  cudaStream_t s = to_stream(stream);
+  const bool k333 = kernel[0] == 3 && kernel[1] == 3 && kernel[2] == 3 && dilation[0] == 1 &&
+                    dilation[1] == 1 && dilation[2] == 1;
+  int32_t* bounds = static_cast<int32_t*>(workspace);
+  uint8_t* region = static_cast<uint8_t*>(workspace) + AUTO_HEADER;
+  // A small table stays in L2 and the two launches that read the box cost more than the grid
+  // saves: below AUTO_GRID_MIN_ROWS rows the hash table is built directly.
+  if (n < AUTO_GRID_MIN_ROWS) {
+    if (k333) return kmap_build_blocks(coords, n, nbr, slots, region, status, s);
+    return kmap_build_voxels(coords, n, kernel, dilation, nbr, slots,
+                             reinterpret_cast<int32_t*>(region), status, s);
+  }
+  // grid capacity: whole 16-byte words of the region after the header
+  const int64_t cap_cells = (int64_t)((workspace_bytes - AUTO_HEADER) / 16) * 4;
+  const int64_t hash_bytes = k333 ? slots * 48 : slots * 4;
+  const int4* c4 = reinterpret_cast<const int4*>(coords);
+  bounds4_init_kernel<<<1, 32, 0, s>>>(bounds);
+  SV_LAUNCH_CHECK();
+  bounds4_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 4 * num_sms()), 256, 0, s>>>(
+      c4, n, bounds);
+  SV_LAUNCH_CHECK();
+  auto_clear_kernel<<<(unsigned)(4 * num_sms()), 256, 0, s>>>(
+      bounds, n, cap_cells, k333, reinterpret_cast<int4*>(region), hash_bytes);
+  SV_LAUNCH_CHECK();
+  auto_insert_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(c4, n, bounds, cap_cells, region,
+                                                                 slots, k333, status);
+  SV_LAUNCH_CHECK();
+  if (k333) {
+    auto_probe333_kernel<<<(unsigned)((n + PROBE_ROWS - 1) / PROBE_ROWS), PROBE_ROWS, 0, s>>>(
+        c4, n, bounds, cap_cells, region, slots, nbr);
+  } else {
+    const int64_t total = n * (int64_t)kernel[0] * kernel[1] * kernel[2];
+    auto_probe_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+        c4, n, bounds, cap_cells, reinterpret_cast<const int32_t*>(region), slots, kernel[0],
+        kernel[1], kernel[2], dilation[0], dilation[1], dilation[2], nbr);
+  }
+  SV_LAUNCH_CHECK();
+  return SV_OK;
+}
+
 extern "C" int64_t sv_conv_plan_tiles(int64_t n) { return n > 0 ? (n + 127) / 128 : 0; }
 
 namespace {
@@ -532,9 +1014,12 @@ size_t plan_tile_cub_bytes(int64_t tiles) {
 extern "C" size_t sv_conv_plan_workspace_bytes(int64_t n) {
   if (n <= 0) return 0;
   const int64_t tiles = sv_conv_plan_tiles(n);
-  // row masks, sorted masks, row ids; tile keys, sorted tile keys, tile ids; CUB scratch
+  // row masks, sorted masks, row ids; tile keys, sorted tile keys, tile ids; CUB scratch (the
+  // one-cluster schedule's run keys and sorted masks for small maps)
   return align_up((size_t)n * 4, 256) * 3 + align_up((size_t)tiles * 4, 256) * 3 +
-         align_up(std::max(plan_cub_bytes(n), plan_tile_cub_bytes(tiles)), 256);
+         align_up(std::max({plan_cub_bytes(n), plan_tile_cub_bytes(tiles),
+                            n <= PLAN_SMALL_ROWS ? (size_t)2 * PLAN_SMALL_ROWS * 4 : (size_t)0}),
+                  256);
 }
 
 extern "C" int sv_conv_plan(const int32_t* nbr, int64_t n, int kvol, int32_t* row_order,
@@ -563,6 +1048,9 @@ extern "C" int sv_conv_plan(const int32_t* nbr, int64_t n, int kvol, int32_t* ro
   size_t cub_bytes = workspace_bytes - (3 * vec + 3 * tvec);
   row_mask_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(nbr, n, kvol, masks, rows);
   SV_LAUNCH_CHECK();
+  if (n <= PLAN_SMALL_ROWS)  // sorted masks and run keys in the sort's scratch
+    return launch_plan_small(masks, n, kvol, reinterpret_cast<uint32_t*>(cub_tmp), row_order,
+                             tile_order, s);
   SV_CUDA_TRY(cub::DeviceRadixSort::SortPairs(cub_tmp, cub_bytes, masks, masks_sorted, rows,
                                               row_order, (int)n, 0, kvol, s));
   if (tile_order != nullptr) {

@@ -180,10 +180,9 @@ class SparseTensor:
         return out.index_put_(index, self.features, accumulate=True)
 
 
-# The dense-grid kernel map pays one host synchronisation (~50 us: the bounding box) and a clear
-# of the grid. Measured on config 5: 2x faster than hashing at 2.7M-10M rows with a box of at
-# most 16 cells per row; below ~1M rows the synchronisation eats the gain.
-GRID_MIN_ROWS = 1 << 20
+# "auto" lets the kernels choose between the dense grid and the hash table on the device (no host
+# synchronisation): the grid when the coordinates' bounding box holds at most this many cells
+# per row. Forcing the grid ("grid") reads the box on the host instead.
 GRID_MAX_CELLS_PER_ROW = 16
 
 # SparseConv3D's AUTO choice of the deduplicated-tile kernel: measured 7-28% faster than the
@@ -212,8 +211,9 @@ def build_neighbor_map(
 
     ``method``: ``"hash"`` (open-addressing table, any coordinates), ``"grid"`` (a dense grid
     of row indices over the coordinates' bounding box; one synchronisation to read the box) or
-    ``"auto"``: the grid for at least GRID_MIN_ROWS rows whose box holds at most
-    GRID_MAX_CELLS_PER_ROW cells per row, the hash table otherwise. Both give the same map.
+    ``"auto"``: the kernels read the box on the device and use the grid when it holds at most
+    GRID_MAX_CELLS_PER_ROW cells per row, the hash table otherwise, without a synchronisation.
+    All three give the same map.
     """
 
     kernel = _triple(kernel_size, "kernel_size")
@@ -235,24 +235,32 @@ def build_neighbor_map(
     status = N.status_word(coords.device)
     if method not in ("auto", "hash", "grid"):
         raise ValueError(f"unknown kernel-map method {method!r}")
-    if table_slots is None and (method == "grid" or (method == "auto" and n >= GRID_MIN_ROWS)):
+    if method == "auto" and table_slots is None:
+        ws_bytes = lib.sv_kmap_auto_workspace_bytes(n)
+        ws = N.workspace(ws_bytes, coords.device)
+        rc = lib.sv_kmap_build_auto(coords.data_ptr(), n, int3(*kernel), int3(*dilations),
+                                    out.data_ptr(), ws.data_ptr(), ws_bytes, status.data_ptr(),
+                                    N.stream(coords.device))
+        N.check(rc, "build_neighbor_map")
+        return out
+    if method == "grid":
         bounds = (ctypes.c_int32 * 8)()
         bws = N.workspace(32, coords.device)
         N.check(lib.sv_coords_bounds(coords.data_ptr(), n, bounds, bws.data_ptr(), 32,
                                      N.stream(coords.device)), "build_neighbor_map")
         extent = [int(bounds[4 + j]) - int(bounds[j]) + 1 for j in range(4)]
-        cells = math.prod(extent)
-        if method == "grid" or (cells <= GRID_MAX_CELLS_PER_ROW * n and cells < 2**31):
-            ext = (ctypes.c_int64 * 4)(*extent)
-            ws_bytes = lib.sv_kmap_grid_workspace_bytes(ext)
-            ws = N.workspace(ws_bytes, coords.device)
-            rc = lib.sv_kmap_build_grid(
-                coords.data_ptr(), n, int3(*kernel), int3(*dilations), out.data_ptr(),
-                (ctypes.c_int32 * 4)(*[int(bounds[j]) for j in range(4)]), ext, ws.data_ptr(),
-                ws_bytes, status.data_ptr(), N.stream(coords.device),
-            )
-            N.check(rc, "build_neighbor_map")
-            return out
+        ext = (ctypes.c_int64 * 4)(*extent)
+        ws_bytes = lib.sv_kmap_grid_workspace_bytes(ext)
+        if ws_bytes == 0:
+            raise ValueError("build_neighbor_map: the coordinates' bounding box is too large for a grid")
+        ws = N.workspace(ws_bytes, coords.device)
+        rc = lib.sv_kmap_build_grid(
+            coords.data_ptr(), n, int3(*kernel), int3(*dilations), out.data_ptr(),
+            (ctypes.c_int32 * 4)(*[int(bounds[j]) for j in range(4)]), ext, ws.data_ptr(),
+            ws_bytes, status.data_ptr(), N.stream(coords.device),
+        )
+        N.check(rc, "build_neighbor_map")
+        return out
     slots = int(table_slots) if table_slots is not None else int(lib.sv_kmap_table_slots(n))
     ws_bytes = lib.sv_kmap_workspace_bytes(slots)
     ws = N.workspace(ws_bytes, coords.device)

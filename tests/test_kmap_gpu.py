@@ -82,13 +82,15 @@ def test_kmap_edge_cases_match_dict_oracle():
 
 def test_block_table_edge_values_match_dict_oracle():
     """The 3x3x3 map goes through the 2x2x2-block table: blocks straddling zero (negative
-    coordinates floor-divide), every corner of the int32 range, a batch index equal to the
-    table's empty marker (0x7F7F7F7F), duplicates spread over several blocks, and a dense random
-    cloud with many duplicates -- all against the reference's dict restated on the CPU."""
+    coordinates floor-divide), every corner of the int32 range, batch index -1 (the empty slot's
+    pattern) and 0x7F7F7F7F, duplicates spread over several blocks, and a dense random cloud with
+    many duplicates -- all against the reference's dict restated on the CPU."""
 
     imax, imin = np.iinfo(np.int32).max, np.iinfo(np.int32).min
-    marker = 0x7F7F7F7F
-    rows = [[marker, 0, 0, 0], [marker, 1, 1, 1], [marker, 0, 0, 0], [marker, -1, 0, 0]]
+    rows = []
+    for marker in (-1, 0x7F7F7F7F):
+        rows += [[marker, 0, 0, 0], [marker, 1, 1, 1], [marker, 0, 0, 0], [marker, -1, 0, 0],
+                 [marker, -1, -1, -1], [marker, -2, -2, -2]]
     for cx in (imin, imin + 1, imax - 1, imax):
         for cy in (imin, imax):
             for cz in (imin + 1, imax - 1):
@@ -139,6 +141,42 @@ def test_conv_row_order_groups_rows_by_mask():
     N.check_device_status(DEV)
 
 
+def _expected_schedule(nbr: np.ndarray):
+    """A stable sort of the row masks, then a stable sort of the 128-row tiles by
+    32 - popcount(union of their masks)."""
+    kvol = nbr.shape[1]
+    masks = ((nbr >= 0).astype(np.int64) << np.arange(kvol)).sum(1)
+    order = np.argsort(masks, kind="stable")
+    m = masks[order]
+    tiles = -(-len(nbr) // 128)
+    keys = np.array([32 - bin(int(np.bitwise_or.reduce(m[t * 128:(t + 1) * 128]))).count("1")
+                     for t in range(tiles)])
+    return order, np.argsort(keys, kind="stable")
+
+
+# Row counts either side of the one-cluster schedule's run length (4096) and row limit (32768,
+# above which the device-wide sort runs), with kernel volumes 27, 9 and 32.
+@pytest.mark.parametrize("n,kvol", [(1, 27), (127, 27), (4096, 27), (4097, 27), (8193, 27),
+                                    (24168, 27), (32768, 27), (32769, 27), (70001, 27),
+                                    (20000, 9), (30000, 32)])
+def test_conv_row_order_is_the_stable_sort(n, kvol):
+    rng = np.random.default_rng(n + kvol)
+    # few distinct masks (long runs of equal keys across the cluster's runs), the all-ones mask
+    # (equal to the padding key of a partial run) and random masks
+    pool = rng.integers(0, 2, size=(40, kvol)).astype(bool)
+    pool[0] = True
+    pool[1] = False
+    pick = rng.integers(0, len(pool), size=n)
+    present = pool[pick]
+    rand = rng.random(n) < 0.2
+    present[rand] = rng.random((int(rand.sum()), kvol)) < 0.7
+    nbr = np.where(present, rng.integers(0, max(n, 1), size=(n, kvol)), -1).astype(np.int32)
+    order_t, tiles_t = conv_row_order(torch.from_numpy(nbr).to(DEV))
+    order, tiles = _expected_schedule(nbr)
+    assert np.array_equal(order_t.cpu().numpy(), order)
+    assert np.array_equal(tiles_t.cpu().numpy(), tiles)
+
+
 # ---- dense-grid kernel map ----------------------------------------------------------------------
 
 
@@ -173,6 +211,48 @@ def test_grid_map_auto_selection_on_dense_and_sparse_boxes():
     sparse[:, 0] *= 100000
     c2 = torch.from_numpy(sparse).to(DEV)
     assert np.array_equal(build_neighbor_map(c2, 3).cpu().numpy(), O.build_neighbor_map(sparse, 3))
+    N.check_device_status(DEV)
+
+
+def _box_rows(shape, n_unique: int, dup: int) -> np.ndarray:
+    """`n_unique` distinct rows in a box of `shape` (batch, c1, c2, c3), both corners occupied,
+    plus `dup` repeated rows, shuffled. Every spatial range starts at an even coordinate and has
+    an even length, so the box is whole 2x2x2 blocks and the block grid of a 3x3x3 map has as
+    many cells as the voxel grid."""
+    rng = np.random.default_rng(dup + n_unique)
+    cells = int(np.prod(shape))
+    flat = rng.choice(cells, size=n_unique - 2, replace=False)
+    b, rest = np.divmod(flat, shape[1] * shape[2] * shape[3])
+    c1, rest = np.divmod(rest, shape[2] * shape[3])
+    c2, c3 = np.divmod(rest, shape[3])
+    lo = np.array([0, -8, 100, -50])
+    rows = np.stack([b, c1, c2, c3], 1) + lo
+    corners = np.array([lo, lo + np.array(shape) - 1])
+    rows = np.concatenate([rows, corners]).astype(np.int32)
+    rows = np.concatenate([rows, rows[rng.choice(n_unique, dup)]])
+    return rows[rng.permutation(len(rows))]
+
+
+# From 2^17 rows the device picks the grid at <= 16 cells per row and the hash table above: a
+# 4 x 64 x 64 x 144 box (2,359,296 cells) with 147,456 rows is exactly 16 cells per row, one row
+# fewer is just above; for the 3x3x3 block path and the general (kernel, dilation) path.
+@pytest.mark.parametrize("dup", [64, 63])
+@pytest.mark.parametrize("ks,dl", [(3, 1), (3, 2), ((3, 1, 5), (1, 2, 1))])
+def test_auto_map_either_side_of_the_grid_limit(dup, ks, dl):
+    rows = _box_rows((4, 64, 64, 144), 147456 - 64, dup)
+    assert len(rows) >= 1 << 17
+    got = _gpu_map(rows, ks, dl)
+    assert np.array_equal(got, O.build_neighbor_map(rows, ks, dl))
+    c = torch.from_numpy(rows).to(DEV)
+    assert np.array_equal(got, build_neighbor_map(c, ks, dl, method="hash").cpu().numpy())
+    N.check_device_status(DEV)
+
+
+# Below 2^17 rows the automatic map always takes the hash table.
+@pytest.mark.parametrize("ks,dl", [(3, 1), (5, 1), ((3, 1, 5), (1, 2, 1))])
+def test_auto_map_small_box(ks, dl):
+    rows = _box_rows((2, 16, 16, 18), 512, 64)
+    assert np.array_equal(_gpu_map(rows, ks, dl), O.build_neighbor_map_dict(rows, ks, dl))
     N.check_device_status(DEV)
 
 
