@@ -183,18 +183,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
-// TMA row gather (no multicast): rows y.x .. y.w of a 2-D tensor map whose box is one row of
-// `box` elements, columns x .. x + box - 1, written as 4 consecutive box rows at dst (in the map's
-// swizzle) and completing on an mbarrier. Rows outside the tensor read the fill value (zero).
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, uint64_t* bar,
-                                            int32_t x, int4 y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-      "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y.x), "r"(y.y), "r"(y.z), "r"(y.w)
-      : "memory");
-}
-
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(dst_smem)),

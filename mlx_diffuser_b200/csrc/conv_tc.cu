@@ -157,10 +157,9 @@ __device__ __forceinline__ void decode_item(const Sched& sc, int32_t item, int32
   *n0 = nt * BN;
 }
 
-template <int BN, int BK, typename T, bool kResidual, int PACK, bool kG4>
+template <int BN, int BK, typename T, bool kResidual, int PACK>
 __global__ void __launch_bounds__(TTHREADS, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                   const __grid_constant__ CUtensorMap tmap_f, const T* __restrict__ feat,
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const T* __restrict__ feat,
                    int n, int cin, const int32_t* __restrict__ nbr, int kvol,
                    const int32_t* __restrict__ row_order, const T* __restrict__ bias,
                    const T* residual, int cout, T* out, Sched sc, int32_t* status) {
@@ -195,8 +194,7 @@ __global__ void __launch_bounds__(TTHREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      // TMA expect_tx arrival of B + (A) 128 cp.async arrivals, or one TMA expect_tx arrival
-      mbar_init(&full[s], kG4 ? 2 : 1 + TBM);
+      mbar_init(&full[s], 1 + TBM);  // TMA expect_tx arrival + 128 cp.async arrivals
       mbar_init(&empty[s], 1);       // tcgen05.commit
     }
     for (int b = 0; b < 2; ++b) {
@@ -289,46 +287,6 @@ __global__ void __launch_bounds__(TTHREADS, 1)
           }
         }
         tc_commit(&acc_full[ab]);  // also after a timeout, so the epilogue never waits on nothing
-      }
-      if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
-    }
-  } else if (warp < 6 && kG4) {
-    // ---- A by TMA row gathers: lanes q = 0..3 of warp 2 load tile rows 32 q .. 32 q + 31 of
-    // each stage, four neighbour rows (one BK-channel box row each) per tile::gather4; a missing
-    // neighbour (-1) is outside the tensor and reads zeros ----
-    if (warp == 2 && lane < 4) {
-      const int q = lane;
-      int it = 0;
-      for (int local = 0; ok; ++local) {
-        const int ws = local & 1;
-        if (!mbar_wait_bounded(&work_full[ws], (local >> 1) & 1, s_abort)) {
-          ok = false;
-          break;
-        }
-        const WorkSlot w = slots[ws];
-        if (w.item < 0) break;
-        const int32_t* nbt = s_nbr + ws * TBM * TMAX_KVOL;  // staged offset-major: [k][128]
-        for (uint32_t m = w.umask; m != 0 && ok; m &= m - 1) {
-          const int k = __ffs(m) - 1;
-          const int4* rows4 = reinterpret_cast<const int4*>(nbt + k * TBM + 32 * q);
-          int4 r4[8];
-#pragma unroll
-          for (int g = 0; g < 8; ++g) r4[g] = rows4[g];
-          for (int kb = 0; kb < kb_per_k; ++kb, ++it) {
-            const int slot = it % S;
-            if (!mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, s_abort)) {
-              ok = false;
-              break;
-            }
-            if (q == 0) mbar_arrive_expect_tx(&full[slot], L::A_STAGE_BYTES);
-            const uint32_t dst =
-                smem_u32(sA + slot * L::A_STAGE_BYTES) + (uint32_t)(32 * q * L::ROW_BYTES);
-#pragma unroll
-            for (int g = 0; g < 8; ++g)
-              tma_gather4(dst + (uint32_t)(4 * g * L::ROW_BYTES), &tmap_f, &full[slot], kb * BK,
-                          r4[g]);
-          }
-        }
       }
       if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
     }
@@ -543,10 +501,7 @@ __global__ void __launch_bounds__(TTHREADS, 1)
           }
         }
         s_orow[ws * TBM + r] = orow;
-        // row-major [128][27] for the cp.async gatherers, offset-major [27][128] for the TMA
-        // row gathers (four consecutive rows of one offset in one 16-byte load)
-        int32_t* nb = s_nbr + ws * TBM * TMAX_KVOL + (kG4 ? r : r * TMAX_KVOL);
-        constexpr int kstride = kG4 ? TBM : 1;
+        int32_t* nb = s_nbr + ws * TBM * TMAX_KVOL + r * TMAX_KVOL;
         const int32_t* nrow = nbr + (int64_t)(orow >= 0 ? orow : 0) * kvol;
 #pragma unroll
         for (int k = 0; k < TMAX_KVOL; ++k) {
@@ -556,7 +511,7 @@ __global__ void __launch_bounds__(TTHREADS, 1)
               report(status, SV_DEVICE_BAD_INDEX);
               v = -1;
             }
-            nb[k * kstride] = v;
+            nb[k] = v;
             mask |= (uint32_t)(v >= 0) << k;
           }
         }
@@ -631,46 +586,21 @@ int weight_map(const ConvArgs& a, bool bf16, int box_k, int box_rows, CUtensorMa
   return SV_OK;
 }
 
-// The features as an (n, Cin) matrix for the row gathers: a box of one row of 64 channels,
-// 128-byte swizzle (the A tile's layout); rows outside [0, n) read zeros.
-int feature_map(const ConvArgs& a, bool bf16, CUtensorMap* tmap) {
-  EncodeTiledFn encode = encode_fn();
-  if (encode == nullptr) SV_FAIL(SV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  const cuuint64_t gdim[2] = {(cuuint64_t)a.cin, (cuuint64_t)a.n};
-  const cuuint64_t gstride[1] = {(cuuint64_t)a.cin * 2};
-  const cuuint32_t box[2] = {64, 1};
-  const cuuint32_t estride[2] = {1, 1};
-  CUresult cr = encode(tmap,
-                       bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                       2, const_cast<void*>(a.features), gdim, gstride, box, estride,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                       CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) SV_FAIL(SV_ERR_CUDA, "cuTensorMapEncodeTiled failed for the features");
-  return SV_OK;
-}
-
-template <int BN, int BK, typename T, bool kResidual, int PACK, bool kG4>
+template <int BN, int BK, typename T, bool kResidual, int PACK>
 int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
-  static_assert(!kG4 || (BK == 64 && PACK == 1), "row gathers load 64-channel rows");
   using L = TcLayout<BN, BK>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   int dev = 0;
   SV_CUDA_TRY(cudaGetDevice(&dev));
   static bool attr_done[256] = {};
   if (dev >= 256 || !attr_done[dev]) {
-    SV_CUDA_TRY(cudaFuncSetAttribute(conv_tc_kernel<BN, BK, T, kResidual, PACK, kG4>,
+    SV_CUDA_TRY(cudaFuncSetAttribute(conv_tc_kernel<BN, BK, T, kResidual, PACK>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
     if (dev < 256) attr_done[dev] = true;
   }
-  CUtensorMap tmap, tmap_f;
-  int rc = weight_map(a, kBF16, BK, BN, &tmap);
+  CUtensorMap tmap;
+  const int rc = weight_map(a, kBF16, BK, BN, &tmap);
   if (rc != SV_OK) return rc;
-  if (kG4) {
-    rc = feature_map(a, kBF16, &tmap_f);
-    if (rc != SV_OK) return rc;
-  } else {
-    tmap_f = tmap;  // unused
-  }
 
   Sched sc;
   sc.counter = counter;
@@ -687,46 +617,30 @@ int launch_bn(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cu
   const int grid = (int)std::min<int64_t>(items, num_sms());
   sc.total_items = (int32_t)items;
   SV_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int32_t), s));
-  conv_tc_kernel<BN, BK, T, kResidual, PACK, kG4><<<grid, TTHREADS, L::SMEM, s>>>(
-      tmap, tmap_f, static_cast<const T*>(a.features), (int)a.n, a.cin, a.nbr, a.kvol,
+  conv_tc_kernel<BN, BK, T, kResidual, PACK><<<grid, TTHREADS, L::SMEM, s>>>(
+      tmap, static_cast<const T*>(a.features), (int)a.n, a.cin, a.nbr, a.kvol,
       a.row_order, static_cast<const T*>(a.bias), static_cast<const T*>(a.residual), a.cout,
       static_cast<T*>(a.out), sc, a.status);
   SV_LAUNCH_CHECK();
   return SV_OK;
 }
 
-template <int BK, typename T, bool kResidual, int PACK, bool kG4>
+template <int BK, typename T, bool kResidual, int PACK>
 int launch_bk(const ConvArgs& a, const int32_t* tile_order, int32_t* counter, cudaStream_t s) {
-  if (a.cout < 32) return launch_bn<16, BK, T, kResidual, PACK, kG4>(a, tile_order, counter, s);
-  if (a.cout % 256 == 0)
-    return launch_bn<256, BK, T, kResidual, PACK, kG4>(a, tile_order, counter, s);
-  if (a.cout % 128 == 0)
-    return launch_bn<128, BK, T, kResidual, PACK, kG4>(a, tile_order, counter, s);
-  if (a.cout % 64 == 0)
-    return launch_bn<64, BK, T, kResidual, PACK, kG4>(a, tile_order, counter, s);
-  return launch_bn<32, BK, T, kResidual, PACK, kG4>(a, tile_order, counter, s);
-}
-
-// A by TMA row gathers (tile::gather4) instead of 16-byte cp.async from four gatherer warps.
-bool use_row_gathers(const ConvArgs& a) {
-#ifdef SV_TC_GATHER4_ALL
-  return a.cin % 64 == 0;
-#else
-  (void)a;
-  return false;
-#endif
+  if (a.cout < 32) return launch_bn<16, BK, T, kResidual, PACK>(a, tile_order, counter, s);
+  if (a.cout % 256 == 0) return launch_bn<256, BK, T, kResidual, PACK>(a, tile_order, counter, s);
+  if (a.cout % 128 == 0) return launch_bn<128, BK, T, kResidual, PACK>(a, tile_order, counter, s);
+  if (a.cout % 64 == 0) return launch_bn<64, BK, T, kResidual, PACK>(a, tile_order, counter, s);
+  return launch_bn<32, BK, T, kResidual, PACK>(a, tile_order, counter, s);
 }
 
 template <typename T, bool kResidual>
 int launch_res(const ConvArgs& a, const int32_t* tile_order, int32_t* counter,
                cudaStream_t s) {
-  if (a.cin == 8) return launch_bk<32, T, kResidual, 4, false>(a, tile_order, counter, s);
-  if (a.cin == 16) return launch_bk<32, T, kResidual, 2, false>(a, tile_order, counter, s);
-  if (a.cin % 64 == 0) {
-    if (use_row_gathers(a)) return launch_bk<64, T, kResidual, 1, true>(a, tile_order, counter, s);
-    return launch_bk<64, T, kResidual, 1, false>(a, tile_order, counter, s);
-  }
-  return launch_bk<32, T, kResidual, 1, false>(a, tile_order, counter, s);
+  if (a.cin == 8) return launch_bk<32, T, kResidual, 4>(a, tile_order, counter, s);
+  if (a.cin == 16) return launch_bk<32, T, kResidual, 2>(a, tile_order, counter, s);
+  if (a.cin % 64 == 0) return launch_bk<64, T, kResidual, 1>(a, tile_order, counter, s);
+  return launch_bk<32, T, kResidual, 1>(a, tile_order, counter, s);
 }
 
 template <typename T>
