@@ -332,7 +332,7 @@ __global__ void tile_cost_kernel(const uint32_t* __restrict__ masks_sorted, int6
 
 // ---- one-cluster schedule for small maps -----------------------------------------------------
 // Up to PLAN_SMALL_ROWS rows the schedule is one launch of a single thread-block cluster, one CTA
-// per run of PLAN_RUN consecutive rows:
+// per run of consecutive rows:
 //   1. each CTA sorts its run's masks (with the row ids) by a block radix sort in registers and
 //      shared memory -- stable, so rows of equal masks keep ascending row order -- and publishes
 //      the sorted keys;
@@ -346,15 +346,22 @@ __global__ void tile_cost_kernel(const uint32_t* __restrict__ masks_sorted, int6
 //      the large path gives.
 // A device-wide sort takes a histogram pass, a scan and four onesweep passes of a few
 // microseconds each however few rows there are; this replaces them and the tile sort.
-// 256 threads x 16 rows per run: a block radix sort's cost grows with the rows one CTA sorts
-// (measured on B200: 4096 rows ~19 us, 8192 rows ~31 us), so more, shorter runs merge faster.
+// Runs of 256 threads x ITEMS rows: a block radix sort's time grows with the rows one CTA sorts
+// (measured on B200: 2048 rows ~12 us, 4096 ~19 us, 8192 ~31 us), so the shortest runs that fit
+// a cluster are used -- 2048 rows (up to 16 CTAs, a non-portable cluster size) where the device
+// can hold such a cluster, else 4096 rows (up to 8, the portable size).
 constexpr int PLAN_THREADS = 256;
-constexpr int PLAN_ITEMS = 16;
-constexpr int PLAN_RUN = PLAN_THREADS * PLAN_ITEMS;
-constexpr int PLAN_MAX_RUNS = 8;  // the portable cluster size
-constexpr int PLAN_SMALL_ROWS = PLAN_RUN * PLAN_MAX_RUNS;
+constexpr int PLAN_SMALL_ROWS = 32768;
 
-using PlanSort = cub::BlockRadixSort<uint32_t, PLAN_THREADS, PLAN_ITEMS, int32_t>;
+template <int ITEMS>
+struct PlanRuns {
+  static constexpr int RUN = PLAN_THREADS * ITEMS;
+  static constexpr int MAX_RUNS = PLAN_SMALL_ROWS / RUN;
+  using Sort = cub::BlockRadixSort<uint32_t, PLAN_THREADS, ITEMS, int32_t>;
+  static size_t smem(int runs) {
+    return std::max(sizeof(typename Sort::TempStorage), (size_t)runs * RUN * 4);
+  }
+};
 
 __device__ __forceinline__ void plan_cluster_sync() {
   __threadfence();  // global writes of this thread before the barrier's release
@@ -363,10 +370,12 @@ __device__ __forceinline__ void plan_cluster_sync() {
       "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+template <int ITEMS>
 __global__ void __launch_bounds__(PLAN_THREADS, 1)
     plan_small_kernel(const uint32_t* __restrict__ masks, int n, int kvol, uint32_t* run_keys,
                       uint32_t* tile_union, int32_t* __restrict__ row_order,
                       int32_t* __restrict__ tile_order) {
+  using R = PlanRuns<ITEMS>;
   extern __shared__ __align__(16) uint8_t plan_smem[];
   const int r = blockIdx.x;  // the grid is one cluster
   const int runs = gridDim.x;
@@ -377,25 +386,25 @@ __global__ void __launch_bounds__(PLAN_THREADS, 1)
   // rows past n sort last: the largest key over the sorted bits, and after any real row of that
   // key by stability (they lie in the last run, after every real row)
   const uint32_t pad = kvol >= 32 ? 0xFFFFFFFFu : (1u << kvol) - 1u;
-  uint32_t key[PLAN_ITEMS];
-  int32_t val[PLAN_ITEMS];
+  uint32_t key[ITEMS];
+  int32_t val[ITEMS];
 #pragma unroll
-  for (int i = 0; i < PLAN_ITEMS; ++i) {
-    const int idx = r * PLAN_RUN + t * PLAN_ITEMS + i;
+  for (int i = 0; i < ITEMS; ++i) {
+    const int idx = r * R::RUN + t * ITEMS + i;
     key[i] = idx < n ? __ldg(&masks[idx]) : pad;
     val[i] = idx;
   }
-  PlanSort(*reinterpret_cast<PlanSort::TempStorage*>(plan_smem)).Sort(key, val, 0, kvol);
-  uint4* mine = reinterpret_cast<uint4*>(run_keys + r * PLAN_RUN + t * PLAN_ITEMS);
+  typename R::Sort(*reinterpret_cast<typename R::Sort::TempStorage*>(plan_smem)).Sort(key, val, 0, kvol);
+  uint4* mine = reinterpret_cast<uint4*>(run_keys + r * R::RUN + t * ITEMS);
 #pragma unroll
-  for (int i = 0; i < PLAN_ITEMS / 4; ++i)
+  for (int i = 0; i < ITEMS / 4; ++i)
     mine[i] = make_uint4(key[4 * i], key[4 * i + 1], key[4 * i + 2], key[4 * i + 3]);
   plan_cluster_sync();
 
   // all runs' sorted keys into shared memory, eight 16-byte loads in flight per thread
   uint32_t* all = reinterpret_cast<uint32_t*>(plan_smem);
   const uint4* src = reinterpret_cast<const uint4*>(run_keys);
-  const int words4 = runs * PLAN_RUN / 4;
+  const int words4 = runs * R::RUN / 4;
   for (int j0 = 0; j0 < words4; j0 += 8 * PLAN_THREADS) {
     uint4 v[8];
 #pragma unroll
@@ -411,26 +420,26 @@ __global__ void __launch_bounds__(PLAN_THREADS, 1)
   }
   __syncthreads();
   // merge ranks, the thread's rows searched together in each other run
-  int pos[PLAN_ITEMS];
+  int pos[ITEMS];
 #pragma unroll
-  for (int i = 0; i < PLAN_ITEMS; ++i) pos[i] = t * PLAN_ITEMS + i;
+  for (int i = 0; i < ITEMS; ++i) pos[i] = t * ITEMS + i;
   for (int rr = 0; rr < runs; ++rr) {
     if (rr == r) continue;
-    const uint32_t* run = all + rr * PLAN_RUN;
+    const uint32_t* run = all + rr * R::RUN;
     const bool inclusive = rr < r;
-    int lo[PLAN_ITEMS];
+    int lo[ITEMS];
 #pragma unroll
-    for (int i = 0; i < PLAN_ITEMS; ++i) lo[i] = 0;
+    for (int i = 0; i < ITEMS; ++i) lo[i] = 0;
 #pragma unroll
-    for (int step = PLAN_RUN >> 1; step > 0; step >>= 1) {
+    for (int step = R::RUN >> 1; step > 0; step >>= 1) {
 #pragma unroll
-      for (int i = 0; i < PLAN_ITEMS; ++i) {
+      for (int i = 0; i < ITEMS; ++i) {
         const uint32_t v = run[lo[i] + step - 1];
         if (v < key[i] || (inclusive && v == key[i])) lo[i] += step;
       }
     }
 #pragma unroll
-    for (int i = 0; i < PLAN_ITEMS; ++i) {
+    for (int i = 0; i < ITEMS; ++i) {
       const uint32_t v = run[lo[i]];
       pos[i] += lo[i] + ((v < key[i] || (inclusive && v == key[i])) ? 1 : 0);
     }
@@ -439,7 +448,7 @@ __global__ void __launch_bounds__(PLAN_THREADS, 1)
   uint32_t acc = 0;
   int acc_tile = -1;
 #pragma unroll
-  for (int i = 0; i < PLAN_ITEMS; ++i) {
+  for (int i = 0; i < ITEMS; ++i) {
     if (pos[i] >= n) continue;
     row_order[pos[i]] = val[i];
     const int tile = pos[i] >> 7;
@@ -469,22 +478,21 @@ __global__ void __launch_bounds__(PLAN_THREADS, 1)
   }
 }
 
-size_t plan_small_smem(int runs) {
-  return std::max(sizeof(PlanSort::TempStorage), (size_t)runs * PLAN_RUN * 4);
-}
-
-// masks: n row masks; scratch: PLAN_SMALL_ROWS words of run keys and the tile unions after them
-// (16-byte aligned).
-int launch_plan_small(const uint32_t* masks, int64_t n, int kvol, uint32_t* scratch,
-                      int32_t* row_order, int32_t* tile_order, cudaStream_t s) {
-  const int runs = (int)((n + PLAN_RUN - 1) / PLAN_RUN);
-  const size_t smem = plan_small_smem(runs);
-  SV_CUDA_TRY(cudaFuncSetAttribute(plan_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)plan_small_smem(PLAN_MAX_RUNS)));
+template <int ITEMS>
+int launch_plan_runs(const uint32_t* masks, int64_t n, int kvol, uint32_t* scratch,
+                     int32_t* row_order, int32_t* tile_order, cudaStream_t s) {
+  using R = PlanRuns<ITEMS>;
+  const int runs = (int)((n + R::RUN - 1) / R::RUN);
+  SV_CUDA_TRY(cudaFuncSetAttribute(plan_small_kernel<ITEMS>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)R::smem(R::MAX_RUNS)));
+  if (R::MAX_RUNS > 8)
+    SV_CUDA_TRY(cudaFuncSetAttribute(plan_small_kernel<ITEMS>,
+                                     cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(runs);
   cfg.blockDim = dim3(PLAN_THREADS);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = R::smem(runs);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -493,9 +501,53 @@ int launch_plan_small(const uint32_t* masks, int64_t n, int kvol, uint32_t* scra
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SV_CUDA_TRY(cudaLaunchKernelEx(&cfg, plan_small_kernel, masks, (int)n, kvol, scratch,
+  SV_CUDA_TRY(cudaLaunchKernelEx(&cfg, plan_small_kernel<ITEMS>, masks, (int)n, kvol, scratch,
                                  scratch + PLAN_SMALL_ROWS, row_order, tile_order));
   return SV_OK;
+}
+
+// Whether this device can run a 16-CTA cluster of the 2048-row kernel (queried once per device).
+bool plan_cluster16_ok() {
+  static int known[256] = {};  // 0 unknown, 1 yes, 2 no
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return false;
+  if (known[dev] == 0) {
+    using R = PlanRuns<8>;
+    bool ok = cudaFuncSetAttribute(plan_small_kernel<8>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)R::smem(R::MAX_RUNS)) == cudaSuccess &&
+              cudaFuncSetAttribute(plan_small_kernel<8>,
+                                   cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                  cudaSuccess;
+    int clusters = 0;
+    if (ok) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(R::MAX_RUNS);
+      cfg.blockDim = dim3(PLAN_THREADS);
+      cfg.dynamicSmemBytes = R::smem(R::MAX_RUNS);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = R::MAX_RUNS;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      ok = cudaOccupancyMaxActiveClusters(&clusters, plan_small_kernel<8>, &cfg) == cudaSuccess &&
+           clusters >= 1;
+    }
+    cudaGetLastError();  // a refused query leaves no error behind
+    known[dev] = ok ? 1 : 2;
+  }
+  return known[dev] == 1;
+}
+
+// masks: n row masks; scratch: PLAN_SMALL_ROWS words of run keys and the tile unions after them
+// (16-byte aligned).
+int launch_plan_small(const uint32_t* masks, int64_t n, int kvol, uint32_t* scratch,
+                      int32_t* row_order, int32_t* tile_order, cudaStream_t s) {
+  if (n <= 8 * PlanRuns<8>::RUN || plan_cluster16_ok())
+    return launch_plan_runs<8>(masks, n, kvol, scratch, row_order, tile_order, s);
+  return launch_plan_runs<16>(masks, n, kvol, scratch, row_order, tile_order, s);
 }
 
 // ---- direct-indexed grid -------------------------------------------------------------------

@@ -154,11 +154,12 @@ def _expected_schedule(nbr: np.ndarray):
     return order, np.argsort(keys, kind="stable")
 
 
-# Row counts either side of the one-cluster schedule's run length (4096) and row limit (32768,
-# above which the device-wide sort runs), with kernel volumes 27, 9 and 32.
-@pytest.mark.parametrize("n,kvol", [(1, 27), (127, 27), (4096, 27), (4097, 27), (8193, 27),
-                                    (24168, 27), (32768, 27), (32769, 27), (70001, 27),
-                                    (20000, 9), (30000, 32)])
+# Row counts either side of the one-cluster schedule's run lengths (2048 and 4096 rows), its
+# switch to 16-CTA clusters (16384) and its row limit (32768, above which the device-wide sort
+# runs), with kernel volumes 27, 9 and 32.
+@pytest.mark.parametrize("n,kvol", [(1, 27), (127, 27), (2048, 27), (2049, 27), (4097, 27),
+                                    (16384, 27), (16385, 27), (24168, 27), (32768, 27),
+                                    (32769, 27), (70001, 27), (20000, 9), (30000, 32)])
 def test_conv_row_order_is_the_stable_sort(n, kvol):
     rng = np.random.default_rng(n + kvol)
     # few distinct masks (long runs of equal keys across the cluster's runs), the all-ones mask
