@@ -485,36 +485,42 @@ __global__ void __launch_bounds__(TTHREADS, 1)
       const bool valid = item < sc.total_items;
       int32_t row_tile = 0, n0 = 0;
       if (valid) decode_item<BN>(sc, item, &row_tile, &n0);
+      // the row and its neighbour list load before the wait for the slot, all TMAX_KVOL loads in
+      // flight together: checking each value before the next load would put a memory latency
+      // per offset on the path to the next item
+      int32_t orow = -1;
+      if (valid) {
+        const int64_t gr = (int64_t)row_tile * TBM + r;
+        if (gr < sc.n_rows) orow = row_order ? __ldg(&row_order[gr]) : (int32_t)gr;
+      }
+      const bool orow_ok = orow >= -1 && orow < n;  // -1: padding between schedule segments
+      const int32_t* nrow = nbr + (int64_t)(orow >= 0 && orow_ok ? orow : 0) * kvol;
+      int32_t nv[TMAX_KVOL];
+#pragma unroll
+      for (int k = 0; k < TMAX_KVOL; ++k)
+        nv[k] = (k < kvol && orow >= 0 && orow_ok) ? __ldg(&nrow[k]) : -1;
       // slot ws (rows, neighbour lists and accumulator) is free once the epilogue has stored
       // the item two back, which also means the gatherers are done with it
       const bool slot_free =
           mbar_wait_bounded(&work_empty[ws], ((local >> 1) & 1) ^ 1, s_abort);
       uint32_t mask = 0;
       if (valid && slot_free) {
-        const int64_t gr = (int64_t)row_tile * TBM + r;
-        int32_t orow = -1;
-        if (gr < sc.n_rows) {
-          orow = row_order ? __ldg(&row_order[gr]) : (int32_t)gr;
-          if (orow < -1 || orow >= n) {  // -1: padding between schedule segments
-            report(status, SV_DEVICE_BAD_INDEX);
-            orow = -1;
-          }
-        }
-        s_orow[ws * TBM + r] = orow;
+        bool bad = !orow_ok;
+        s_orow[ws * TBM + r] = orow_ok ? orow : -1;
         int32_t* nb = s_nbr + ws * TBM * TMAX_KVOL + r * TMAX_KVOL;
-        const int32_t* nrow = nbr + (int64_t)(orow >= 0 ? orow : 0) * kvol;
 #pragma unroll
         for (int k = 0; k < TMAX_KVOL; ++k) {
           if (k < kvol) {
-            int32_t v = orow >= 0 ? __ldg(&nrow[k]) : -1;
+            int32_t v = nv[k];
             if (v >= n) {
-              report(status, SV_DEVICE_BAD_INDEX);
+              bad = true;
               v = -1;
             }
             nb[k] = v;
             mask |= (uint32_t)(v >= 0) << k;
           }
         }
+        if (bad) report(status, SV_DEVICE_BAD_INDEX);
       }
       mask = __reduce_or_sync(0xffffffffu, mask);
       if (lane == 0) s_wmask[warp - 10] = mask;

@@ -438,34 +438,39 @@ __global__ void __launch_bounds__(FTHREADS, 1)
         row_tile = sc.tile_order ? __ldg(&sc.tile_order[t]) : t;
         n0 = nt * BN;
       }
+      // the row and its neighbour list load before the wait for the slot, all FMAX_KVOL loads in
+      // flight together
+      int32_t orow = -1;
+      if (valid) {
+        const int64_t gr = (int64_t)row_tile * FBM + r;
+        if (gr < sc.n_rows) orow = row_order ? __ldg(&row_order[gr]) : (int32_t)gr;
+      }
+      const bool orow_ok = orow >= -1 && orow < n;  // -1: padding between schedule segments
+      const int32_t* nrow = nbr + (int64_t)(orow >= 0 && orow_ok ? orow : 0) * kvol;
+      int32_t nv[FMAX_KVOL];
+#pragma unroll
+      for (int k = 0; k < FMAX_KVOL; ++k)
+        nv[k] = (k < kvol && orow >= 0 && orow_ok) ? __ldg(&nrow[k]) : -1;
       const bool slot_free =
           mbar_wait_bounded(&work_empty[ws], ((local >> 1) & 1) ^ 1, s_abort);
       uint32_t mask = 0;
       if (valid && slot_free) {
-        const int64_t gr = (int64_t)row_tile * FBM + r;
-        int32_t orow = -1;
-        if (gr < sc.n_rows) {
-          orow = row_order ? __ldg(&row_order[gr]) : (int32_t)gr;
-          if (orow < -1 || orow >= n) {
-            report(status, SV_DEVICE_BAD_INDEX);
-            orow = -1;
-          }
-        }
-        s_orow[ws * FBM + r] = orow;
+        bool bad = !orow_ok;
+        s_orow[ws * FBM + r] = orow_ok ? orow : -1;
         int32_t* nbw = s_nbr + ws * FBM * FMAX_KVOL + r * FMAX_KVOL;
-        const int32_t* nrow = nbr + (int64_t)(orow >= 0 ? orow : 0) * kvol;
 #pragma unroll
         for (int k = 0; k < FMAX_KVOL; ++k) {
           if (k < kvol) {
-            int32_t v = orow >= 0 ? __ldg(&nrow[k]) : -1;
+            int32_t v = nv[k];
             if (v >= n) {
-              report(status, SV_DEVICE_BAD_INDEX);
+              bad = true;
               v = -1;
             }
             nbw[k] = v;
             mask |= (uint32_t)(v >= 0) << k;
           }
         }
+        if (bad) report(status, SV_DEVICE_BAD_INDEX);
       }
       mask = __reduce_or_sync(0xffffffffu, mask);
       if (lane == 0) s_wmask[warp - 10] = mask;
