@@ -725,7 +725,8 @@ def map_timing(args, dev, flush, coords):
     c = torch.from_numpy(coords).to(dev)
     n = len(coords)
     ms = _time_device(lambda: build_neighbor_map(c, 3), args.steps, args.warmup, flush)
-    return ms, _hbm_roofline(16.0 * n + 4.0 * 27 * n, ms, "kmap_insert + kmap_probe")
+    return ms, _hbm_roofline(16.0 * n + 4.0 * 27 * n, ms,
+                             "sv_kmap_build_auto (box, clear, insert, probe)")
 
 
 def cpu_conv_sample(coords, feats, w_kio, rows: int, seed: int = 0) -> dict:
@@ -1214,7 +1215,7 @@ def hbm_lines(args, dev, flush) -> list:
         return sparse_downsample(x, 2)
 
     cases = [
-        ("kernel-map build", "kmap_insert_kernel + kmap_probe_kernel",
+        ("kernel-map build", "bounds4 + auto_clear + auto_insert + auto_probe333",
          lambda: build_neighbor_map(coords, 3), 16.0 * n + 4.0 * 27 * n, n),
         ("sparse_downsample", "pool (coords sort + segment mean)", fresh_down,
          16.0 * n + 16.0 * m + 4.0 * n + 2.0 * 128 * (n + m), n),
