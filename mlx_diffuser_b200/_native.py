@@ -182,7 +182,15 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream(device: torch.device) -> int:
+    """The device's current CUDA stream handle (what torch launches its own kernels on)."""
+
+    if _raw_stream is not None:
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        return _raw_stream(index)
     return torch.cuda.current_stream(device).cuda_stream
 
 

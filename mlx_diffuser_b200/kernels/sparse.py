@@ -32,6 +32,10 @@ def _check_shapes(features, neighbors, weights, bias) -> None:
         raise ValueError(f"bias must have shape ({weights.shape[2]},), got {tuple(bias.shape)}")
 
 
+# sv_conv3d_workspace_bytes by argument tuple (a pure function of the shapes)
+_WS_BYTES: dict[tuple, int] = {}
+
+
 def conv3d_forward(
     features: torch.Tensor,
     neighbors: torch.Tensor,
@@ -63,7 +67,13 @@ def conv3d_forward(
         return out
     dcode = N.DTYPE_CODE[features.dtype]
     lib = N.load()
-    ws_bytes = lib.sv_conv3d_workspace_bytes(n, cin, cout, kvol, dcode, layout, algo)
+    size_key = (n, cin, cout, kvol, dcode, layout, algo)
+    ws_bytes = _WS_BYTES.get(size_key)
+    if ws_bytes is None:
+        ws_bytes = lib.sv_conv3d_workspace_bytes(n, cin, cout, kvol, dcode, layout, algo)
+        if len(_WS_BYTES) > 1024:
+            _WS_BYTES.clear()
+        _WS_BYTES[size_key] = ws_bytes
     ws = N.workspace(ws_bytes, dev) if ws_bytes else None
     if residual is not None and (tuple(residual.shape) != (n, cout)
                                  or residual.dtype != features.dtype

@@ -387,9 +387,10 @@ class SparseConv3D(nn.Module):
         self.conv = _SparseConv3DCore(in_channels, out_channels, kernel_size, bias)
         self._operand_cache: tuple[Any, torch.Tensor, torch.Tensor] | None = None
 
-    def _operands(self, device: torch.device, dtype: torch.dtype):
-        weight = self.conv.weight
-        bias = self.conv.bias if hasattr(self.conv, "bias") else self.conv._bias
+    def _operands(self, device: torch.device, dtype: torch.dtype, weight=None, bias=None):
+        if weight is None:
+            weight = self.conv.weight
+            bias = self.conv.bias if hasattr(self.conv, "bias") else self.conv._bias
         if (
             weight.device == device
             and weight.dtype == dtype
@@ -422,8 +423,9 @@ class SparseConv3D(nn.Module):
         if features.ndim != 2:
             raise ValueError(f"features must be 2D, got {tuple(features.shape)}")
         N.require_cuda(features, "features")
-        w_param = self.conv.weight
-        b_param = self.conv.bias if hasattr(self.conv, "bias") else self.conv._bias
+        core = self.conv
+        w_param = core.weight
+        b_param = core.bias if hasattr(core, "bias") else core._bias
         if torch.is_grad_enabled() and (features.requires_grad or w_param.requires_grad
                                         or b_param.requires_grad):
             # training: differentiable casts, gradients from the library's backward kernels
@@ -440,7 +442,7 @@ class SparseConv3D(nn.Module):
             if residual is not None:
                 out = out + residual
             return x.replace(out)
-        weight, bias = self._operands(features.device, features.dtype)
+        weight, bias = self._operands(features.device, features.dtype, w_param, b_param)
         o, _, _, _, i = weight.shape
         if features.shape[1] != i or neighbors.shape[0] != features.shape[0]:
             raise ValueError(
