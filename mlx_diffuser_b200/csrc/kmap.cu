@@ -1,12 +1,15 @@
-// Kernel-map construction: coordinate hash table, K-offset neighbour probe, and the
-// mask-grouped row schedule for the tensor-core convolution.
+// Kernel-map construction (hash tables and dense grids, neighbour probes) and the mask-grouped
+// row schedule for the tensor-core convolution.
 //
 // Restates build_neighbor_map (src/mlx_diffuser/layers/sparse.py:146-175) on the GPU:
-//  * the reference's dict keyed by the 4-tuple (b, c1, c2, c3) becomes an open-addressing
-//    table whose slots hold only a row index (4 bytes); a slot's key is the coordinate row it
-//    points at, so keys are exact for every int32 value (no packing, no range limit);
+//  * the reference's dict keyed by the 4-tuple (b, c1, c2, c3) becomes one of three exact
+//    structures, for every int32 value (no packing, no range limit): a dense grid of row indices
+//    over the coordinates' bounding box (for 3x3x3 maps, a grid of 2x2x2 blocks); an
+//    open-addressing table of 2x2x2 blocks keyed by their full 16-byte coordinates (3x3x3,
+//    dilation 1); or one of single voxels whose slots hold a row index (other kernels).
+//    sv_kmap_build_auto picks between the grid and the table on the device;
 //  * "a later duplicate overwrites an earlier one" (the dict comprehension, :159) becomes
-//    atomicMax on the slot: the largest row index among equal rows wins;
+//    atomicMax on the cell or slot: the largest row index among equal rows wins;
 //  * offsets are enumerated in the reference's order (:160-169); a neighbour coordinate that
 //    leaves the int32 range simply misses, as a Python dict lookup of that tuple would.
 #include <algorithm>
