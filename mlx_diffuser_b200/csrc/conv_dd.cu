@@ -46,7 +46,9 @@ namespace {
 constexpr int DTBM = 128;     // tile rows == TMEM lanes
 constexpr int DKVOL = 27;     // 3 x 3 x 3 only
 constexpr int DTHREADS = 448;
-constexpr int DEDUP_BYTES = 64 * 1024;  // one source-row buffer
+// One source-row buffer: 448 rows at 64 input channels (p99 of a Morton tile's distinct rows on
+// surface scenes is ~450), leaving room for 6 two-offset B stages.
+constexpr int DEDUP_BYTES = 56 * 1024;
 constexpr int LOADER_BAR = 2;           // named barrier of the four loader warps
 
 __host__ __device__ constexpr int dd_umax(int cin) { return DEDUP_BYTES / (cin * 2); }
@@ -207,10 +209,16 @@ size_t dd_sort_bytes(int64_t n) {
 
 // ---- the convolution --------------------------------------------------------------------------
 
-template <int BN>
+// P: 64-channel K blocks per pipeline stage. At 64 input channels two offsets share a stage
+// (8 MMAs and one commit, 16 KB of B for BN = 64), so a stage's fixed costs -- barrier round
+// trips, the commit, the A builders' TMEM store wait -- and the B loads' latency are spread over
+// twice the MMA work.
+template <int BN, int P>
 struct DdLayout {
-  static constexpr int STAGES = BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
-  static constexpr int B_STAGE_BYTES = BN * 128;
+  static constexpr int STAGES = P == 2 ? 6 : BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
+  static constexpr int B_SUB_BYTES = BN * 128;  // one 64-channel block of B
+  static constexpr int B_STAGE_BYTES = P * B_SUB_BYTES;
+  static constexpr uint32_t A_STAGE_COLS = 32 * P;  // TMEM columns of one stage's A
   static constexpr int B_OFF = 0;
   static constexpr int DEDUP_OFF = B_OFF + STAGES * B_STAGE_BYTES;
   static constexpr int LNBR_OFF = DEDUP_OFF + 2 * DEDUP_BYTES;
@@ -225,7 +233,7 @@ struct DdLayout {
   static constexpr uint32_t ACC_COLS = 2 * BN;
   static constexpr uint32_t A_COL0 = ACC_COLS;
   static constexpr uint32_t TMEM_COLS = 512;
-  static_assert(A_COL0 + 32 * STAGES <= TMEM_COLS, "TMEM budget");
+  static_assert(A_COL0 + A_STAGE_COLS * STAGES <= TMEM_COLS, "TMEM budget");
   static_assert(B_STAGE_BYTES % 1024 == 0, "swizzle atoms");
   static_assert(LNBR_BYTES % 16 == 0, "16-byte copies of the local map");
   static_assert(BAR_OFF % 8 == 0, "mbarrier alignment");
@@ -312,13 +320,30 @@ __device__ __forceinline__ uint32_t dd_pack2(float lo, float hi) {
   }
 }
 
+// The item's 64-channel K blocks in order: offsets of the mask, KB blocks each.
+struct SubStages {
+  uint32_t m;
+  int kb;
+  __device__ __forceinline__ bool next(int KB, int* k, int* b) {
+    if (m == 0) return false;
+    *k = __ffs(m) - 1;
+    *b = kb;
+    if (++kb == KB) {
+      kb = 0;
+      m &= m - 1;
+    }
+    return true;
+  }
+};
+
 template <int BN, int CIN, typename T, bool kResidual>
 __global__ void __launch_bounds__(DTHREADS, 1)
     conv_dd_kernel(const __grid_constant__ CUtensorMap tmap_w, const T* __restrict__ feat,
                    int n, const int32_t* __restrict__ nbr, PlanView plan,
                    const T* __restrict__ bias, const T* residual, int cout, T* out, DdSched sc,
                    int32_t* status) {
-  using L = DdLayout<BN>;
+  constexpr int P = (CIN == 64 && BN <= 64) ? 2 : 1;
+  using L = DdLayout<BN, P>;
   constexpr int S = L::STAGES;
   constexpr int UMAX = dd_umax(CIN);
   constexpr int ROWB = CIN * 2;
@@ -388,18 +413,20 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         }
         const DdSlot w = slots[ws];
         if (w.item < 0) break;
-        for (uint32_t m = w.umask; m != 0 && ok; m &= m - 1) {
-          const int k = __ffs(m) - 1;
-          for (int kb = 0; kb < KB; ++kb, ++it) {
-            const int slot = it % S;
-            if (!mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, s_abort)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&full[slot], L::B_STAGE_BYTES);
-            tma_load_2d(smem_u32(sB + slot * L::B_STAGE_BYTES), &tmap_w, &full[slot],
-                        k * CIN + kb * 64, w.n0);
+        SubStages sub{w.umask, 0};
+        for (; ok; ++it) {
+          int k[P], kb[P], cnt = 0;
+          for (int j = 0; j < P && sub.next(KB, &k[j], &kb[j]); ++j) ++cnt;
+          if (cnt == 0) break;
+          const int slot = it % S;
+          if (!mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, s_abort)) {
+            ok = false;
+            break;
           }
+          mbar_arrive_expect_tx(&full[slot], (uint32_t)(cnt * L::B_SUB_BYTES));
+          for (int j = 0; j < cnt; ++j)
+            tma_load_2d(smem_u32(sB + slot * L::B_STAGE_BYTES + j * L::B_SUB_BYTES), &tmap_w,
+                        &full[slot], k[j] * CIN + kb[j] * 64, w.n0);
         }
       }
       if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
@@ -425,23 +452,27 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(ab * BN);
         int first = 1;
-        for (uint32_t m = w.umask; m != 0 && ok; m &= m - 1) {
-          for (int kb = 0; kb < KB; ++kb, ++it) {
-            const int slot = it % S;
-            if (!mbar_wait_bounded(&full[slot], (it / S) & 1, s_abort)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t a0 = tmem + L::A_COL0 + (uint32_t)(slot * 32);
-            const uint32_t b0 = smem_u32(sB + slot * L::B_STAGE_BYTES);
+        SubStages sub{w.umask, 0};
+        for (; ok; ++it) {
+          int k, kb, cnt = 0;
+          for (int j = 0; j < P && sub.next(KB, &k, &kb); ++j) ++cnt;
+          if (cnt == 0) break;
+          const int slot = it % S;
+          if (!mbar_wait_bounded(&full[slot], (it / S) & 1, s_abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int j = 0; j < cnt; ++j) {
+            const uint32_t a0 = tmem + L::A_COL0 + (uint32_t)(slot * L::A_STAGE_COLS + j * 32);
+            const uint32_t b0 = smem_u32(sB + slot * L::B_STAGE_BYTES + j * L::B_SUB_BYTES);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               tc_mma_ts_f16(d, a0 + (uint32_t)(kk * 8), smem_desc_kmajor(b0 + kk * 32, 2u, 128u),
                             idesc, (first && kk == 0) ? 0u : 1u);
             first = 0;
-            tc_commit(&empty[slot]);
           }
+          tc_commit(&empty[slot]);
         }
         tc_commit(&acc_full[ab]);  // also after a timeout, so the epilogue never waits on nothing
       }
@@ -639,19 +670,6 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       const int16_t* ln = s_lnbr + ws * DTBM * DKVOL + r * DKVOL;
       const uint32_t buf = smem_u32(sDedup + ws * DEDUP_BYTES);
       const int32_t orow = s_orow[ws * DTBM + r];
-      // stages of the item in order: offsets of the mask, KB 64-channel blocks each
-      uint32_t m = w.umask;
-      int kb_next = 0;
-      auto next_stage = [&](int* k, int* kb) -> bool {
-        if (m == 0) return false;
-        *k = __ffs(m) - 1;
-        *kb = kb_next;
-        if (++kb_next == KB) {
-          kb_next = 0;
-          m &= m - 1;
-        }
-        return true;
-      };
       // the row of (offset k, block kb) into v: chunk j of a buffer row sits at j ^ (slot & 7)
       auto load_stage = [&](uint32_t (&v)[32], int k, int kb) {
         const int e = ln[k];
@@ -688,41 +706,35 @@ __global__ void __launch_bounds__(DTHREADS, 1)
           }
         }
       };
-      // wait for the stage's TMEM slot, store the row into it, signal the MMA
-      auto store_stage = [&](const uint32_t (&v)[32]) -> bool {
+      // Each stage: wait for its TMEM slot, store its first row (read while the previous stage
+      // finished), read and store its second row behind the first store, wait for both stores,
+      // signal the MMA; then read the next stage's first row.
+      SubStages sub{w.umask, 0};
+      uint32_t va[32], vb[32];
+      int k, kb;
+      bool has = sub.next(KB, &k, &kb);
+      if (has) load_stage(va, k, kb);
+      while (has && ok) {
         const int slot = it % S;
         if (!__all_sync(0xffffffffu,
-                        mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, s_abort)))
-          return false;
+                        mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, s_abort))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        tmem_st_32x32b_x32(t_lane + (uint32_t)(slot * 32), v);
+        const uint32_t t_stage = t_lane + (uint32_t)(slot * L::A_STAGE_COLS);
+        tmem_st_32x32b_x32(t_stage, va);
+        if (P == 2 && sub.next(KB, &k, &kb)) {
+          load_stage(vb, k, kb);
+          tmem_st_32x32b_x32(t_stage + 32u, vb);
+        }
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_dd(&full[slot]);
         ++it;
-        return true;
-      };
-      uint32_t va[32], vb[32];
-      int k, kb;
-      bool has = next_stage(&k, &kb);
-      if (has) load_stage(va, k, kb);
-      while (has && ok) {
-        has = next_stage(&k, &kb);
-        if (has) load_stage(vb, k, kb);
-        __syncwarp();
-        if (!store_stage(va)) {
-          ok = false;
-          break;
-        }
-        if (!has) break;
-        has = next_stage(&k, &kb);
+        has = sub.next(KB, &k, &kb);
         if (has) load_stage(va, k, kb);
-        __syncwarp();
-        if (!store_stage(vb)) {
-          ok = false;
-          break;
-        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive_dd(&slot_empty[ws]);
@@ -759,7 +771,7 @@ EncodeTiledFnDd encode_fn_dd() {
 template <int BN, int CIN, typename T, bool kResidual>
 int launch_dd(const ConvArgs& a, PlanView plan, int64_t tiles, int32_t* counter,
               cudaStream_t s) {
-  using L = DdLayout<BN>;
+  using L = DdLayout<BN, (CIN == 64 && BN <= 64) ? 2 : 1>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   int dev = 0;
   SV_CUDA_TRY(cudaGetDevice(&dev));

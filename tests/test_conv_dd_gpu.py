@@ -4,7 +4,7 @@
 
 The plan is integer data and is compared exactly: tiles of 128 rows in (batch, Morton) order,
 each tile's distinct source rows in that order too, every local-map entry pointing at its source
-row (or -1 / -2 for a missing neighbour / a row the 64 KB buffer could not hold)."""
+row (or -1 / -2 for a missing neighbour / a row the 56 KB buffer could not hold)."""
 
 from __future__ import annotations
 
@@ -56,7 +56,7 @@ def decode_plan(plan: DedupPlan):
     lib = N.load()
     n, cin = plan.n, plan.cin
     tiles = (n + 127) // 128
-    umax = 65536 // (2 * cin)
+    umax = 56 * 1024 // (2 * cin)  # rows one shared-memory buffer of the kernel holds
     raw = plan.buffer.cpu().numpy()
     align = lambda v: (v + 255) // 256 * 256  # noqa: E731
     o = 0
