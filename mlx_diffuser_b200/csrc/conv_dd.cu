@@ -13,14 +13,18 @@
 // kernel gathers each of them once into shared memory and builds every A operand from there.
 //
 // Per work item (one 128-row tile x BN output channels):
-//   warps 2-5   loaders: take the next item from the persistent scheduler, publish its output
-//               rows and offset mask, then cp.async its local map [128][27] (int16) and its
-//               unique source rows (CIN * 2 bytes each, at most 64 KB) into one of two buffers;
-//   warps 10-13 A builders, one tile row per thread: for each (offset, 64-channel block) read
-//               the row's 128 bytes from the shared buffer (chunks XOR-swizzled by the slot, so
-//               the sources of neighbouring rows -- consecutive slots -- use different bank
-//               groups) and store them with tcgen05.st into a TMEM stage (32 columns: 64
-//               bf16/fp16 values per lane); the next stage's row is read while this one waits;
+//   warps 2-5   loaders: take the next item from the persistent scheduler, read its plan
+//               record, output rows and source-row indices, cp.async its local map [128][27]
+//               (int16) and its unique source rows (CIN * 2 bytes each, at most 56 KB) into one
+//               of two buffers once the A builders are done with it, then publish its output
+//               rows and offset mask once the epilogue is done with the previous ones;
+//   warps 10-   A builders, two groups of four warps at 64 input channels, three at 128; in a
+//               group one tile row per thread, and group g takes the stages whose index is g
+//               modulo the group count: for each (offset, 64-channel block) read the row's
+//               128 bytes from the shared buffer (chunks XOR-swizzled by the slot, so the sources
+//               of neighbouring rows -- consecutive slots -- use different bank groups) and
+//               store them with tcgen05.st into a TMEM stage (32 columns: 64 bf16/fp16 values
+//               per lane); the group's next row is read while this one's store completes;
 //   warp 0      TMA producer: the B tile W[k][kb*64 : +64, n0 : n0+BN] per stage (as conv_tc);
 //   warp 1      TMEM allocator and MMA issuer: tcgen05.mma with A from TMEM, B from shared
 //               memory (4 x K=16 per stage), accumulators double-buffered in TMEM;
@@ -45,7 +49,14 @@ namespace {
 
 constexpr int DTBM = 128;     // tile rows == TMEM lanes
 constexpr int DKVOL = 27;     // 3 x 3 x 3 only
-constexpr int DTHREADS = 448;
+constexpr int DLT = 128;         // loader threads (warps 2-5)
+constexpr int DEPI0 = 6;         // first epilogue warp
+constexpr int DBLD0 = 10;        // first A-builder warp
+// A-builder groups of four warps; group g builds the pipeline stages whose index is g modulo the
+// group count. One group alone waits on its own TMEM stores and shared-memory reads; two (three
+// at 128 input channels, where a stage is one offset) keep stages in flight while it waits.
+__host__ __device__ constexpr int dd_groups(int cin) { return cin == 64 ? 2 : 3; }
+__host__ __device__ constexpr int dd_threads(int cin) { return 32 * (DBLD0 + 4 * dd_groups(cin)); }
 // One source-row buffer: 448 rows at 64 input channels (p99 of a Morton tile's distinct rows on
 // surface scenes is ~450), leaving room for 6 two-offset B stages.
 constexpr int DEDUP_BYTES = 56 * 1024;
@@ -227,7 +238,7 @@ struct DdLayout {
   static constexpr int SLOT_OFF = OROW_OFF + 2 * DTBM * 4;
   static constexpr int MISC_OFF = SLOT_OFF + 2 * 16;
   static constexpr int BAR_OFF = MISC_OFF + 32;
-  static constexpr int NUM_BARS = 2 * STAGES + 10;
+  static constexpr int NUM_BARS = 2 * STAGES + 12;
   static constexpr int BYTES = BAR_OFF + NUM_BARS * 8;
   static constexpr int SMEM = BYTES + 1024;
   static constexpr uint32_t ACC_COLS = 2 * BN;
@@ -262,10 +273,10 @@ __device__ __forceinline__ bool loader_bar_any(bool pred) {
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.or.pred p, %2, 128, q;\n\t"
+      "bar.red.or.pred p, %2, %3, q;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(r)
-      : "r"((uint32_t)pred), "n"(LOADER_BAR)
+      : "r"((uint32_t)pred), "n"(LOADER_BAR), "n"(DLT)
       : "memory");
   return r != 0;
 }
@@ -337,12 +348,13 @@ struct SubStages {
 };
 
 template <int BN, int CIN, typename T, bool kResidual>
-__global__ void __launch_bounds__(DTHREADS, 1)
+__global__ void __launch_bounds__(dd_threads(CIN), 1)
     conv_dd_kernel(const __grid_constant__ CUtensorMap tmap_w, const T* __restrict__ feat,
                    int n, const int32_t* __restrict__ nbr, PlanView plan,
                    const T* __restrict__ bias, const T* residual, int cout, T* out, DdSched sc,
                    int32_t* status) {
   constexpr int P = (CIN == 64 && BN <= 64) ? 2 : 1;
+  constexpr int DGROUPS = dd_groups(CIN);
   using L = DdLayout<BN, P>;
   constexpr int S = L::STAGES;
   constexpr int UMAX = dd_umax(CIN);
@@ -364,13 +376,14 @@ __global__ void __launch_bounds__(DTHREADS, 1)
   // One arrival per warp wherever a warp finishes a step together (after __syncwarp): an
   // mbarrier takes its arrivals one at a time, and 128 per stage cost more than a narrow
   // stage's MMAs.
-  uint64_t* full = bars;                     // [S]: TMA expect_tx + 4 A-builder warps
+  uint64_t* full = bars;                     // [S]: TMA expect_tx + one group's 4 builder warps
   uint64_t* empty = bars + S;                // [S]: tcgen05.commit
   uint64_t* acc_full = bars + 2 * S;         // [2]: tcgen05.commit
   uint64_t* acc_empty = acc_full + 2;        // [2]: 4 epilogue warps
   uint64_t* meta_full = acc_empty + 2;       // [2]: the first loader (rows, slot published)
   uint64_t* dedup_full = meta_full + 2;      // [2]: 128 loaders' cp.async (local map + rows)
-  uint64_t* slot_empty = dedup_full + 2;     // [2]: 4 A-builder warps + 4 epilogue warps
+  uint64_t* buf_empty = dedup_full + 2;      // [2]: the A-builder warps (local map + rows read)
+  uint64_t* meta_empty = buf_empty + 2;      // [2]: 4 epilogue warps (output rows read)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -384,8 +397,9 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
       mbar_init(&meta_full[b], 1);
-      mbar_init(&dedup_full[b], DTBM);
-      mbar_init(&slot_empty[b], 8);
+      mbar_init(&dedup_full[b], DLT);
+      mbar_init(&buf_empty[b], 4 * DGROUPS);
+      mbar_init(&meta_empty[b], 4);
     }
     *s_abort = 0;
     fence_mbar_init();
@@ -478,12 +492,12 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       }
       if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
     }
-  } else if (warp < 6) {
+  } else if (warp < DEPI0) {
     // ---- loaders ----
     // CPR 16-byte chunks per source row; loader g copies chunk g % CPR of buffer rows
     // g / CPR + RPP * i (a warp instruction writes 32 / CPR whole rows: conflict-free)
     constexpr int CPR = ROWB / 16;
-    constexpr int RPP = 128 / CPR;
+    constexpr int RPP = DLT / CPR;
     const int g = threadIdx.x - 64;
     const int chunk = g % CPR;
     const int row0 = g / CPR;
@@ -497,15 +511,81 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       }
       const int32_t item = *s_fetch;
       const bool valid = item < sc.total_items;
-      const bool slot_free = mbar_wait_bounded(&slot_empty[ws], ((local >> 1) & 1) ^ 1, s_abort);
-      const bool fail = loader_bar_any(!slot_free);
+      // Everything that does not need the buffer is read before waiting for it: the tile's
+      // output rows, its plan record and the first batch of source-row indices.
+      constexpr int ORPT = (DTBM + DLT - 1) / DLT;
+      constexpr int PASSES = (UMAX + RPP - 1) / RPP;
+      constexpr int BATCH = PASSES > 28 ? 28 : PASSES;
       int32_t tile = 0;
       int4 meta = make_int4(0, 0, 0, 0);
-      if (valid && !fail) {
-        const int32_t nt = item / sc.tiles;
+      int32_t orows[ORPT];
+      int32_t srows[BATCH];
+      const int32_t nt = valid ? item / sc.tiles : 0;
+      if (valid) {
         tile = item - nt * sc.tiles;
-        s_orow[ws * DTBM + g] = __ldg(&plan.rows[(int64_t)tile * DTBM + g]);
+#pragma unroll
+        for (int j = 0; j < ORPT; ++j) {
+          const int i = g + j * DLT;
+          orows[j] = i < DTBM ? __ldg(&plan.rows[(int64_t)tile * DTBM + i]) : -1;
+        }
         meta = __ldg(&plan.meta[tile]);
+      }
+      const int count = min(meta.x, UMAX);
+      const int32_t* src_rows = plan.src + (int64_t)tile * UMAX;
+#pragma unroll
+      for (int i = 0; i < BATCH; ++i) {
+        const int r = row0 + RPP * i;
+        srows[i] = r < count ? __ldg(&src_rows[r]) : -1;
+      }
+      // The local map and rows go into the buffer as soon as the A builders are done with it;
+      // the output rows and the slot record wait for the epilogue of the tile that used them.
+      const uint32_t ph = ((local >> 1) & 1) ^ 1;
+      bool fail = loader_bar_any(!mbar_wait_bounded(&buf_empty[ws], ph, s_abort));
+      if (valid && !fail) {
+        const uint32_t lnbr_dst = smem_u32(s_lnbr + ws * DTBM * DKVOL);
+        const uint8_t* lnbr_src =
+            reinterpret_cast<const uint8_t*>(plan.lnbr + (int64_t)tile * DTBM * DKVOL);
+#pragma unroll
+        for (int c = g; c < L::LNBR_BYTES / 16; c += DLT)
+          cp_async_16(lnbr_dst + (uint32_t)(c * 16), lnbr_src + c * 16, 16u);
+        const uint32_t buf = smem_u32(sDedup + ws * DEDUP_BYTES);
+#pragma unroll 1
+        for (int i0 = 0; i0 < PASSES && row0 + RPP * i0 < count; i0 += BATCH) {
+          if (i0 > 0) {
+#pragma unroll
+            for (int i = 0; i < BATCH; ++i) {
+              const int r = row0 + RPP * (i0 + i);
+              srows[i] = r < count ? __ldg(&src_rows[r]) : -1;
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < BATCH; ++i) {
+            const int r = row0 + RPP * (i0 + i);
+            if (r >= count) break;
+            int32_t srow = srows[i];
+            uint32_t bytes = 16u;
+            if (srow < 0 || srow >= n) {
+              report(status, SV_DEVICE_BAD_INDEX);
+              srow = 0;
+              bytes = 0u;
+            }
+            // chunk c of buffer row r lands at (c & ~7) | ((c ^ r) & 7): the 16-byte chunks of
+            // each 128-byte half are XOR-swizzled by the row's slot
+            const int pos = (chunk & ~7) | ((chunk ^ r) & 7);
+            cp_async_16(buf + (uint32_t)(r * ROWB + pos * 16),
+                        feat + (int64_t)srow * CIN + chunk * 8, bytes);
+          }
+        }
+        cp_async_arrive_noinc(&dedup_full[ws]);
+      }
+      const bool meta_free = fail || mbar_wait_bounded(&meta_empty[ws], ph, s_abort);
+      fail = loader_bar_any(fail || !meta_free);
+      if (valid && !fail) {
+#pragma unroll
+        for (int j = 0; j < ORPT; ++j) {
+          const int i = g + j * DLT;
+          if (i < DTBM) s_orow[ws * DTBM + i] = orows[j];
+        }
         if (g == 0) {
           DdSlot w;
           w.item = item;
@@ -522,53 +602,16 @@ __global__ void __launch_bounds__(DTHREADS, 1)
         w.tile = 0;
         slots[ws] = w;
       }
-      asm volatile("bar.sync %0, 128;" ::"n"(LOADER_BAR) : "memory");
+      asm volatile("bar.sync %0, %1;" ::"n"(LOADER_BAR), "n"(DLT) : "memory");
       if (g == 0) mbar_arrive_dd(&meta_full[ws]);
       if (fail) ok = false;
       if (!valid || fail) break;
-      // local map and distinct source rows of the tile
-      const uint32_t lnbr_dst = smem_u32(s_lnbr + ws * DTBM * DKVOL);
-      const uint8_t* lnbr_src =
-          reinterpret_cast<const uint8_t*>(plan.lnbr + (int64_t)tile * DTBM * DKVOL);
-#pragma unroll
-      for (int c = g; c < L::LNBR_BYTES / 16; c += DTBM)
-        cp_async_16(lnbr_dst + (uint32_t)(c * 16), lnbr_src + c * 16, 16u);
-      const uint32_t buf = smem_u32(sDedup + ws * DEDUP_BYTES);
-      const int32_t* src_rows = plan.src + (int64_t)tile * UMAX;
-      const int count = min(meta.x, UMAX);
-      // every source index first (independent loads in flight together), then the copies: an
-      // index load behind each copy would wait a full memory latency per row
-      constexpr int PASSES = UMAX / RPP;
-      int32_t srows[PASSES];
-#pragma unroll
-      for (int i = 0; i < PASSES; ++i) {
-        const int r = row0 + RPP * i;
-        srows[i] = r < count ? __ldg(&src_rows[r]) : -1;
-      }
-#pragma unroll
-      for (int i = 0; i < PASSES; ++i) {
-        const int r = row0 + RPP * i;
-        if (r >= count) break;
-        int32_t srow = srows[i];
-        uint32_t bytes = 16u;
-        if (srow < 0 || srow >= n) {
-          report(status, SV_DEVICE_BAD_INDEX);
-          srow = 0;
-          bytes = 0u;
-        }
-        // chunk c of buffer row r lands at (c & ~7) | ((c ^ r) & 7): the 16-byte chunks of each
-        // 128-byte half are XOR-swizzled by the row's slot
-        const int pos = (chunk & ~7) | ((chunk ^ r) & 7);
-        cp_async_16(buf + (uint32_t)(r * ROWB + pos * 16), feat + (int64_t)srow * CIN + chunk * 8,
-                    bytes);
-      }
-      cp_async_arrive_noinc(&dedup_full[ws]);
     }
     if (!ok) {
       cp_async_wait_all();
       report(status, SV_DEVICE_WAIT_TIMEOUT);
     }
-  } else if (warp < 10) {
+  } else if (warp < DBLD0) {
     // ---- epilogue: warp w reads TMEM lanes 32*(w % 4) .. +31 ----
     const int q = warp & 3;
     const int er = q * 32 + lane;
@@ -641,15 +684,16 @@ __global__ void __launch_bounds__(DTHREADS, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_dd(&acc_empty[ab]);
-        mbar_arrive_dd(&slot_empty[ws]);
+        mbar_arrive_dd(&meta_empty[ws]);
       }
     }
     if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
   } else {
-    // ---- A builders: tile row r = 32 * (warp % 4) + lane, TMEM lane r ----
-    // Software-pipelined: the next stage's row is read from the shared buffer (or, for a row the
-    // buffer could not hold, from global memory) before this stage waits for its TMEM slot.
+    // ---- A builders: tile row r = 32 * (warp % 4) + lane, TMEM lane r; group grp ----
+    // Software-pipelined: the group's next stage's row is read from the shared buffer (or, for a
+    // row the buffer could not hold, from global memory) before that stage waits for its slot.
     const int q = warp & 3;
+    const int grp = (warp - DBLD0) >> 2;
     const int r = q * 32 + lane;
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16) + L::A_COL0;
     int it = 0;
@@ -706,38 +750,63 @@ __global__ void __launch_bounds__(DTHREADS, 1)
           }
         }
       };
-      // Each stage: wait for its TMEM slot, store its first row (read while the previous stage
-      // finished), read and store its second row behind the first store, wait for both stores,
-      // signal the MMA; then read the next stage's first row.
+      // Stages of the tile in order; this group builds those whose global index it0 + s is
+      // congruent to its group number. Each stage: wait for its TMEM slot, store its first row
+      // (read while the group's previous stage finished), read and store its second row behind
+      // the first store, wait for both stores, signal the MMA; then read the group's next first
+      // row.
       SubStages sub{w.umask, 0};
       uint32_t va[32], vb[32];
-      int k, kb;
-      bool has = sub.next(KB, &k, &kb);
-      if (has) load_stage(va, k, kb);
-      while (has && ok) {
-        const int slot = it % S;
+      int k[P], kb[P];
+      auto take = [&]() {
+        int c = 0;
+        for (int j = 0; j < P && sub.next(KB, &k[j], &kb[j]); ++j) ++c;
+        return c;
+      };
+      const int it0 = it;
+      int s = 0;
+      int cnt = take();
+      while (cnt > 0 && ((it0 + s) % DGROUPS) != grp) {
+        ++s;
+        cnt = take();
+      }
+      if (cnt > 0) load_stage(va, k[0], kb[0]);
+      while (cnt > 0 && ok) {
+        const int gi = it0 + s;
+        const int slot = gi % S;
         if (!__all_sync(0xffffffffu,
-                        mbar_wait_bounded(&empty[slot], ((it / S) & 1) ^ 1, s_abort))) {
+                        mbar_wait_bounded(&empty[slot], ((gi / S) & 1) ^ 1, s_abort))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t t_stage = t_lane + (uint32_t)(slot * L::A_STAGE_COLS);
         tmem_st_32x32b_x32(t_stage, va);
-        if (P == 2 && sub.next(KB, &k, &kb)) {
-          load_stage(vb, k, kb);
-          tmem_st_32x32b_x32(t_stage + 32u, vb);
+        if constexpr (P == 2) {
+          if (cnt == 2) {
+            load_stage(vb, k[P - 1], kb[P - 1]);
+            tmem_st_32x32b_x32(t_stage + 32u, vb);
+          }
         }
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_dd(&full[slot]);
-        ++it;
-        has = sub.next(KB, &k, &kb);
-        if (has) load_stage(va, k, kb);
+        ++s;
+        cnt = take();
+        while (cnt > 0 && ((it0 + s) % DGROUPS) != grp) {
+          ++s;
+          cnt = take();
+        }
+        if (cnt > 0) load_stage(va, k[0], kb[0]);
       }
+      while (cnt > 0) {  // after an expired wait: keep the stage count in step
+        ++s;
+        cnt = take();
+      }
+      it = it0 + s;
       __syncwarp();
-      if (lane == 0) mbar_arrive_dd(&slot_empty[ws]);
+      if (lane == 0) mbar_arrive_dd(&buf_empty[ws]);
     }
     if (!ok) report(status, SV_DEVICE_WAIT_TIMEOUT);
   }
@@ -802,7 +871,7 @@ int launch_dd(const ConvArgs& a, PlanView plan, int64_t tiles, int32_t* counter,
   sc.total_items = (int32_t)items;
   const int grid = (int)std::min<int64_t>(items, num_sms());
   SV_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int32_t), s));
-  conv_dd_kernel<BN, CIN, T, kResidual><<<grid, DTHREADS, L::SMEM, s>>>(
+  conv_dd_kernel<BN, CIN, T, kResidual><<<grid, dd_threads(CIN), L::SMEM, s>>>(
       tmap, static_cast<const T*>(a.features), (int)a.n, a.nbr, plan,
       static_cast<const T*>(a.bias), static_cast<const T*>(a.residual), a.cout,
       static_cast<T*>(a.out), sc, a.status);

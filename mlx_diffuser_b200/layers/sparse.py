@@ -185,12 +185,13 @@ class SparseTensor:
 # per row. Forcing the grid ("grid") reads the box on the host instead.
 GRID_MAX_CELLS_PER_ROW = 16
 
-# SparseConv3D's AUTO choice of the deduplicated-tile kernel: measured 7-28% faster than the
-# mask-sorted kernel at 64 input channels on every scene tried from 3 neighbours per row up
-# (surfaces with 17-25, uniform 8% and 30% occupancy), and slower at 128 input channels; a very
-# sparse map (a tile then visits offsets that few of its rows use) keeps the mask-sorted kernel.
+# SparseConv3D's AUTO choice of the deduplicated-tile kernel: measured 11-36% faster than the
+# mask-sorted kernel at 64 input channels on surfaces (17-23 neighbours per row) and on uniform
+# 30% occupancy (8.7), and slower at 128 input channels; a sparse map (uniform 8% occupancy,
+# 3 neighbours per row: 0.158 against 0.117 ms) keeps the mask-sorted kernel, since a tile then
+# visits offsets that few of its rows use.
 DEDUP_CIN = (64,)
-DEDUP_MIN_PAIRS_PER_ROW = 2.5
+DEDUP_MIN_PAIRS_PER_ROW = 6.0
 
 
 def build_neighbor_map(
