@@ -27,7 +27,8 @@
 //               per lane); the group's next row is read while this one's store completes;
 //   warp 0      TMA producer: the B tile W[k][kb*64 : +64, n0 : n0+BN] per stage (as conv_tc);
 //   warp 1      TMEM allocator and MMA issuer: tcgen05.mma with A from TMEM, B from shared
-//               memory (4 x K=16 per stage), accumulators double-buffered in TMEM;
+//               memory (4 x K=16 per 64-channel block, up to four blocks and one commit per
+//               stage), accumulators double-buffered in TMEM;
 //   warps 6-9   epilogue (as conv_tc): tcgen05.ld, + bias (+ residual), round, store.
 // A local-map entry is the row's slot in the shared buffer, -1 for a missing neighbour, or -2
 // when the tile had more distinct rows than the buffer holds: that row is then read from global
@@ -220,13 +221,18 @@ size_t dd_sort_bytes(int64_t n) {
 
 // ---- the convolution --------------------------------------------------------------------------
 
-// P: 64-channel K blocks per pipeline stage. At 64 input channels two offsets share a stage
-// (8 MMAs and one commit, 16 KB of B for BN = 64), so a stage's fixed costs -- barrier round
-// trips, the commit, the A builders' TMEM store wait -- and the B loads' latency are spread over
-// twice the MMA work.
+// P: 64-channel K blocks per pipeline stage. At 64 input channels and BN <= 64 four offsets
+// share a stage (16 MMAs and one commit, 32 KB of B for BN = 64; three such stages fill TMEM
+// beside the two accumulators). Each stage carries a fixed cost -- the commit and the pipeline
+// drain it waits for, the barrier round trips, the builders' TMEM store wait -- that measured
+// ~700 cycles against ~42 per 128 x 64 x 16 MMA, so fewer, larger stages pay.
+__host__ __device__ constexpr int dd_blocks_per_stage(int cin, int bn) {
+  return (cin == 64 && bn <= 64) ? 4 : 1;
+}
+
 template <int BN, int P>
 struct DdLayout {
-  static constexpr int STAGES = P == 2 ? 6 : BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
+  static constexpr int STAGES = P == 4 ? 3 : BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
   static constexpr int B_SUB_BYTES = BN * 128;  // one 64-channel block of B
   static constexpr int B_STAGE_BYTES = P * B_SUB_BYTES;
   static constexpr uint32_t A_STAGE_COLS = 32 * P;  // TMEM columns of one stage's A
@@ -353,7 +359,7 @@ __global__ void __launch_bounds__(dd_threads(CIN), 1)
                    int n, const int32_t* __restrict__ nbr, PlanView plan,
                    const T* __restrict__ bias, const T* residual, int cout, T* out, DdSched sc,
                    int32_t* status) {
-  constexpr int P = (CIN == 64 && BN <= 64) ? 2 : 1;
+  constexpr int P = dd_blocks_per_stage(CIN, BN);
   constexpr int DGROUPS = dd_groups(CIN);
   using L = DdLayout<BN, P>;
   constexpr int S = L::STAGES;
@@ -782,10 +788,19 @@ __global__ void __launch_bounds__(dd_threads(CIN), 1)
         tc_fence_after();
         const uint32_t t_stage = t_lane + (uint32_t)(slot * L::A_STAGE_COLS);
         tmem_st_32x32b_x32(t_stage, va);
-        if constexpr (P == 2) {
-          if (cnt == 2) {
-            load_stage(vb, k[P - 1], kb[P - 1]);
-            tmem_st_32x32b_x32(t_stage + 32u, vb);
+        // the stage's other blocks, alternately into vb and va; a register array is refilled
+        // only after its previous TMEM store has completed
+#pragma unroll
+        for (int j = 1; j < P; ++j) {
+          if (j < cnt) {
+            if (j >= 2) tc_wait_st();
+            if (j & 1) {
+              load_stage(vb, k[j], kb[j]);
+              tmem_st_32x32b_x32(t_stage + 32u * j, vb);
+            } else {
+              load_stage(va, k[j], kb[j]);
+              tmem_st_32x32b_x32(t_stage + 32u * j, va);
+            }
           }
         }
         tc_wait_st();
@@ -840,7 +855,7 @@ EncodeTiledFnDd encode_fn_dd() {
 template <int BN, int CIN, typename T, bool kResidual>
 int launch_dd(const ConvArgs& a, PlanView plan, int64_t tiles, int32_t* counter,
               cudaStream_t s) {
-  using L = DdLayout<BN, (CIN == 64 && BN <= 64) ? 2 : 1>;
+  using L = DdLayout<BN, dd_blocks_per_stage(CIN, BN)>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   int dev = 0;
   SV_CUDA_TRY(cudaGetDevice(&dev));
