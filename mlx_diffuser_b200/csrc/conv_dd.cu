@@ -59,7 +59,7 @@ constexpr int DBLD0 = 10;        // first A-builder warp
 __host__ __device__ constexpr int dd_groups(int cin) { return cin == 64 ? 2 : 3; }
 __host__ __device__ constexpr int dd_threads(int cin) { return 32 * (DBLD0 + 4 * dd_groups(cin)); }
 // One source-row buffer: 448 rows at 64 input channels (p99 of a Morton tile's distinct rows on
-// surface scenes is ~450), leaving room for 6 two-offset B stages.
+// surface scenes is ~450), leaving room for three four-offset B stages (96 KB).
 constexpr int DEDUP_BYTES = 56 * 1024;
 constexpr int LOADER_BAR = 2;           // named barrier of the four loader warps
 
