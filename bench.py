@@ -56,7 +56,8 @@ def parse_args():
         "print one line each: kmap = kernel-map build on 16 x 128^3 at 8%% occupancy; pool = "
         "downsample + upsample of the 237k-voxel 128^3 scene at 128 channels; scene128 = "
         "convs 64->64->32 on that scene; sweep = map build and conv over occupancy "
-        "{0.5, 2, 8, 30}%% x grid {64, 128}^3 x width {32, 128, 512, 1024}, batch 16; halo = "
+        "{0.5, 2, 8, 30}%% x grid {64, 128}^3 x width {32, 128, 512, 1024}, batch 16 (under "
+        "torchrun the 16 batch elements are sharded over the ranks, strong scaling); halo = "
         "the 128^3 scene Morton-partitioned over the torchrun ranks (strong scaling), convs "
         "64->64->32 each after an NCCL halo exchange; topology = occupancy -> coords on 16 x 64^3 "
         "logits, sparse_subdivide and 8^3 attention windows of the 128^3 scene; resblock = the SLat "
@@ -70,6 +71,11 @@ def parse_args():
         "the narrow-channel convs (config 4's scene128, config 3's 128->128, config 5's shell and "
         "uniform cells at 64/128 channels) with the deduplicated-tile kernel and the "
         "mask-sorted tcgen05 kernel side by side",
+    )
+    p.add_argument(
+        "--sweep-cells",
+        default="",
+        help="sweep only these (grid:occupancy) cells, e.g. '64:0.08,128:0.02' (default: all)",
     )
     p.add_argument(
         "--profiling",
@@ -1016,6 +1022,99 @@ def link_ceiling(coords_h, feats_h, out_h, out_d, c_d, f_d, dev, reps: int = 10)
             "d2h_gbs": reps * d2h / (start.elapsed_time(e_out) * 1e-3) / 1e9}
 
 
+SWEEP_BATCH = 16
+SWEEP_CELLS = [(g, o) for g in (64, 128) for o in (0.005, 0.02, 0.08, 0.30)]
+SWEEP_WIDTHS = (32, 128, 512, 1024)
+
+
+def sweep_cells(args) -> list:
+    """The (grid, occupancy) cells of the sweep, all of them or those ``--sweep-cells`` names."""
+
+    if not args.sweep_cells:
+        return list(SWEEP_CELLS)
+    cells = []
+    for item in args.sweep_cells.split(","):
+        g, o = item.split(":")
+        cells.append((int(g), float(o)))
+    return cells
+
+
+def sweep_scene(grid: int, occ: float):
+    """One sweep cell: ``SWEEP_BATCH`` uniform scenes of ``grid``^3 at occupancy ``occ``."""
+
+    from mlx_diffuser_b200 import scenes
+
+    return scenes.batched([scenes.uniform(grid, occ, 700 + b) for b in range(SWEEP_BATCH)])
+
+
+def batch_shard(coords: np.ndarray, batch: int, world: int, rank: int) -> np.ndarray:
+    """Rank ``rank``'s share of a ``batch``-element scene set under batch sharding: the elements
+    [rank * batch // world, (rank + 1) * batch // world), with their batch index rebased to 0."""
+
+    if not 1 <= world <= batch or not 0 <= rank < world:
+        raise ValueError(f"batch sharding needs 1 <= world ({world}) <= batch ({batch})")
+    lo, hi = rank * batch // world, (rank + 1) * batch // world
+    sel = (coords[:, 0] >= lo) & (coords[:, 0] < hi)
+    out = np.ascontiguousarray(coords[sel])
+    out[:, 0] -= lo
+    return out
+
+
+def run_sweep_sharded(args) -> None:
+    """``--workload sweep`` under torchrun: each cell's 16 batch elements are split over the
+    ranks (no communication in the path). Every rank times its own share with CUDA events; the
+    line gives the whole batch's voxels over the slowest rank's time (strong scaling)."""
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def slowest(ms: float) -> float:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def total(v: int) -> int:
+        t = torch.tensor([v], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return int(t.item())
+
+    for grid, occ in sweep_cells(args):
+        full = sweep_scene(grid, occ)
+        mine = batch_shard(full, SWEEP_BATCH, world, rank)
+        dist.barrier(device_ids=[local_rank])
+        ms_map = slowest(map_timing(args, dev, flush, mine)[0])
+        for ch in SWEEP_WIDTHS:
+            # the same rule on every rank (it reads the whole batch), so all take the same steps
+            if len(full) * ch / world > 4_000_000_000:
+                continue
+            dist.barrier(device_ids=[local_rank])
+            ms, pairs, x, _ = conv_timing(args, dev, flush, mine, ch, ch, torch.bfloat16, 13)
+            del x
+            ms = slowest(ms)
+            pairs = total(pairs)
+            if rank == 0:
+                line = _line("sparse conv3d active-voxels/s", len(full) / (ms * 1e-3), "voxels/s",
+                             ms, args,
+                             {"workload": f"uniform{grid}x16_{occ:g}_c{ch}_bf16",
+                              "voxels": len(full), "valid_pairs": pairs, "kmap_ms": ms_map,
+                              "parallelism": f"batch-sharded x{world}"})
+                line["n_gpus"] = world
+                line["scaling"] = "strong"
+                print(json.dumps(line), flush=True)
+            torch.cuda.empty_cache()
+    dist.barrier(device_ids=[local_rank])
+    dist.destroy_process_group()
+
+
 def run_workload(args) -> None:
     import torch
 
@@ -1073,20 +1172,19 @@ def run_workload(args) -> None:
                                {"workload": f"scene128_conv{cin}to{cout}_bf16",
                                 "voxels": len(coords), "valid_pairs": pairs}, roof))
     elif args.workload == "sweep":
-        for grid in (64, 128):
-            for occ in (0.005, 0.02, 0.08, 0.30):
-                coords = scenes.batched([scenes.uniform(grid, occ, 700 + b) for b in range(16)])
-                ms_map, roof_map = map_case(coords)
-                for ch in (32, 128, 512, 1024):
-                    if len(coords) * ch > 4_000_000_000:
-                        continue  # keep features and output under 8 GB each
-                    ms, pairs, _, roof = conv_case(coords, ch, ch, torch.bfloat16, 13)
-                    lines.append(_line(
-                        "sparse conv3d active-voxels/s", len(coords) / (ms * 1e-3), "voxels/s",
-                        ms, args,
-                        {"workload": f"uniform{grid}x16_{occ:g}_c{ch}_bf16",
-                         "voxels": len(coords), "valid_pairs": pairs, "kmap_ms": ms_map,
-                         "kmap_roofline": roof_map}, roof))
+        for grid, occ in sweep_cells(args):
+            coords = sweep_scene(grid, occ)
+            ms_map, roof_map = map_case(coords)
+            for ch in SWEEP_WIDTHS:
+                if len(coords) * ch > 4_000_000_000:
+                    continue  # keep features and output under 8 GB each
+                ms, pairs, _, roof = conv_case(coords, ch, ch, torch.bfloat16, 13)
+                lines.append(_line(
+                    "sparse conv3d active-voxels/s", len(coords) / (ms * 1e-3), "voxels/s",
+                    ms, args,
+                    {"workload": f"uniform{grid}x16_{occ:g}_c{ch}_bf16",
+                     "voxels": len(coords), "valid_pairs": pairs, "kmap_ms": ms_map,
+                     "kmap_roofline": roof_map}, roof))
     elif args.workload == "topology":
         from mlx_diffuser_b200.layers.sparse import attention_windows, occupied_coordinates, sparse_subdivide
 
@@ -1631,6 +1729,8 @@ def main() -> None:
         run_reference(args)
     elif args.workload == "halo":
         run_halo(args)
+    elif args.workload == "sweep" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_sweep_sharded(args)
     elif args.workload != "conv1024":
         run_workload(args)
     else:

@@ -1,5 +1,6 @@
 """Host-side logic of bench.py that needs no GPU: binding a rank to its GPU's local CPUs
-(through a fake NVML) and giving the CPU baseline the full CPU set back afterwards."""
+(through a fake NVML) and giving the CPU baseline the full CPU set back afterwards, and the
+batch sharding of the occupancy/width sweep over torchrun ranks."""
 
 from __future__ import annotations
 
@@ -7,6 +8,7 @@ import os
 import sys
 import types
 
+import numpy as np
 import pytest
 import torch
 
@@ -72,3 +74,37 @@ def test_binding_is_a_no_op_without_nvml_or_when_all_cpus_are_local(monkeypatch,
     monkeypatch.setitem(sys.modules, "pynvml", _fake_nvml(allowed))
     bench.bind_to_gpu_cpus(0)
     assert os.sched_getaffinity(0) == allowed and bench._HOST_CPUS is None
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8, 16])
+def test_sweep_batch_shards_partition_the_batch(world):
+    """Every sweep element lands on exactly one rank, in order, its batch index rebased to 0 on
+    that rank: the shards together are the whole batch."""
+
+    from mlx_diffuser_b200 import scenes
+
+    full = scenes.batched([scenes.uniform(16, 0.05, 700 + b) for b in range(bench.SWEEP_BATCH)])
+    parts = [bench.batch_shard(full, bench.SWEEP_BATCH, world, r) for r in range(world)]
+    assert sum(len(p) for p in parts) == len(full)
+    rebuilt = []
+    for r, p in enumerate(parts):
+        lo = r * bench.SWEEP_BATCH // world
+        hi = (r + 1) * bench.SWEEP_BATCH // world
+        assert p.dtype == full.dtype and p.flags.c_contiguous
+        assert set(np.unique(p[:, 0])) == set(range(hi - lo))
+        q = p.copy()
+        q[:, 0] += lo
+        rebuilt.append(q)
+    assert np.array_equal(np.concatenate(rebuilt), full)
+
+
+def test_sweep_batch_shard_rejects_more_ranks_than_elements_and_parses_cells():
+    full = np.zeros((4, 4), np.int32)
+    with pytest.raises(ValueError):
+        bench.batch_shard(full, 4, 5, 0)
+    with pytest.raises(ValueError):
+        bench.batch_shard(full, 4, 2, 2)
+    args = types.SimpleNamespace(sweep_cells="")
+    assert bench.sweep_cells(args) == bench.SWEEP_CELLS
+    args.sweep_cells = "64:0.08,128:0.02"
+    assert bench.sweep_cells(args) == [(64, 0.08), (128, 0.02)]
